@@ -1,0 +1,511 @@
+"""FPV2 prefill-layer benchmark on B200 (one process per GPU).
+
+A *step* is one FlashPrefill V2 attention layer at 64k tokens (
+Qwen3-4B-shaped, Hq=32, Hkv=8, head_dim 128, bf16, alpha=0.1, correction on,
+topic-block synthetic inputs): the fused index stage (pool K/V, score, select,
+compact) followed by the tcgen05 sparse attention, through the public
+``fpv2.fpv2_sdpa`` call with inputs resident in HBM. With N > 1 GPUs the layer
+is split head-parallel (Hkv/N KV heads and their query heads per GPU) and the
+output is re-assembled with one NCCL all-gather; total work is fixed (strong
+scaling) and ``value`` is the whole layer's retained TFLOP/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
+
+``--impl reference`` times the reference's algorithm on the host cores: the
+CPU restatement in oracle/fpv2_oracle.py (the reference itself needs MLX on an
+Apple GPU), on a bounded sample of the same layer, in the same unit.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from dataclasses import replace
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "flashprefillv2-mlx_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "sparse prefill-attn ms/layer & TFLOP/s (retained) at 64k; % bf16 peak; selection GB/s"
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+CONFIGS = {
+    # name: (length, Hq, Hkv, head_dim, dtype, alpha)
+    "c3": (65536, 32, 8, 128, torch.bfloat16, 0.1),
+    "c2": (16384, 32, 8, 128, torch.bfloat16, 0.1),
+    "c5": (131072, 64, 8, 128, torch.float16, 0.1),
+}
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+
+def load_peaks() -> tuple[dict, str]:
+    if PEAKS_FILE.exists():
+        return json.loads(PEAKS_FILE.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def retained_attention_flops(sel_ids, sel_counts, pr_counts, *, G, tile_q, block_k, offset,
+                             valid_lq, valid_lk, D, corr) -> float:
+    """4*D * sum over (kv head, tile) of causal (q, k) pairs of the selected blocks
+    (all G heads) plus, with correction, G * (valid rows) * pruned entries."""
+    ids = sel_ids.cpu().numpy()
+    cnt = sel_counts.cpu().numpy()
+    pcnt = pr_counts.cpu().numpy()
+    hkv, nt, nb = ids.shape
+    total = 0.0
+    for h in range(hkv):
+        for t in range(nt):
+            row0 = t * tile_q
+            rows = np.arange(row0, min(row0 + tile_q, valid_lq))
+            if rows.size == 0:
+                continue
+            pos = offset + rows
+            blocks = ids[h, t, : cnt[h, t]]
+            starts = blocks.astype(np.int64) * block_k
+            ends = np.minimum(starts + block_k, valid_lk)
+            # causal keys of each row inside each block
+            pairs = np.clip(np.minimum(pos[None, :] + 1, ends[:, None]) - starts[:, None], 0, None)
+            total += float(pairs.sum()) * G
+            if corr:
+                total += float(rows.size) * G * float(pcnt[h, t])
+    return 4.0 * D * total
+
+
+def index_stage_bytes(Hq, Hkv, L, D, Nt, Nb, esize=2) -> int:
+    """Algorithmic HBM bytes of the fused index stage: read Q, K, V; write pooled K/V,
+    two full-width int32 lists and two count arrays."""
+    return (Hq * L * D * esize + 2 * Hkv * L * D * esize + 2 * Hkv * Nb * D * esize
+            + 2 * Hkv * Nt * Nb * 4 + 2 * Hkv * Nt * 4)
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="fpv2_clocks_", suffix=".csv")
+            os.close(fd)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self, load_fraction: float = 0.5) -> dict:
+        if self.proc is None or self.path is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags)
+                          if f.lower() == "active"})
+        sm = [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU leg: the reference algorithm (oracle port) on a bounded sample
+# ---------------------------------------------------------------------------
+
+
+def cpu_sample(q, k, v, cfg, *, tiles_per_step: int, head: int = 0, seed_tile: int | None = None):
+    """Run the oracle's index stage + blockwise attention for ``tiles_per_step``
+    tiles of KV head ``head`` (latest tiles, the heaviest) and return
+    (seconds, retained FLOPs, description)."""
+    from oracle import fpv2_oracle as O
+
+    hq, L, D = q.shape
+    hkv = k.shape[0]
+    G = hq // hkv
+    nt = L // cfg.tile_q
+    last = nt if seed_tile is None else seed_tile
+    tiles = list(range(max(0, last - tiles_per_step), last))
+    qh = q[head * G:(head + 1) * G].float().numpy()
+    kh = k[head:head + 1].float().numpy()
+    vh = v[head:head + 1].float().numpy()
+    t0 = time.perf_counter()
+    pk = O.pool_blocks(kh, cfg.block_k, "bf16")
+    pv = O.pool_blocks(vh, cfg.block_k, "bf16")
+    # selection for the sampled tiles only: slice their rows (offset keeps positions)
+    row0 = tiles[0] * cfg.tile_q
+    rows = slice(row0, (tiles[-1] + 1) * cfg.tile_q)
+    c = replace(O.as_config(cfg), score_chunk_tiles=8,
+                last_n_blocks=max(0, cfg.last_n_blocks - (nt - 1 - tiles[-1])))
+    sel = O.block_scores_and_select(qh[:, rows], pk, scale=D ** -0.5, config=c, offset=row0).selected
+    lists = O.compact_block_indices(sel, config=c, offset=row0, query_length=qh[:, rows].shape[1],
+                                    key_length=L)
+    out = O.sparse_attention(qh[:, rows], kh, vh, pk, pv, *lists, scale=D ** -0.5, config=c,
+                             offset=row0, dtype="bf16")
+    dt = time.perf_counter() - t0
+    assert np.isfinite(out).all()
+    flops = retained_attention_flops(torch.from_numpy(lists[0]), torch.from_numpy(lists[1]),
+                                     torch.from_numpy(lists[3]), G=G, tile_q=c.tile_q,
+                                     block_k=c.block_k, offset=row0,
+                                     valid_lq=qh[:, rows].shape[1], valid_lk=L, D=D,
+                                     corr=c.mean_correction)
+    desc = (f"KV head {head}, tiles {tiles[0]}..{tiles[-1]} ({len(tiles)} of {nt} per head, "
+            f"{len(tiles) * G * cfg.tile_q} query rows): oracle pool + select + compact + "
+            f"list-driven attention, numpy float32")
+    return dt, flops, desc
+
+
+# ---------------------------------------------------------------------------
+# main
+# ---------------------------------------------------------------------------
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c3")
+    ap.add_argument("--no-corr", action="store_true", help="mean correction off")
+    ap.add_argument("--alpha", type=float, default=None)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-tiles", type=int, default=256, help="tiles per CPU sample")
+    return ap.parse_args(argv)
+
+
+def dist_setup(n: int):
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    length, Hq, Hkv, D, dtype, alpha = CONFIGS[args.config]
+    if args.alpha is not None:
+        alpha = args.alpha
+    import fpv2
+    from fpv2.patch import _effective_config
+    from tests.synthetic import topic_qkv
+
+    base_cfg = fpv2.FPV2Config(alpha=alpha, mean_correction=not args.no_corr)
+    cfg = _effective_config(base_cfg, Hq, Hkv)
+    scale = D ** -0.5
+
+    if args.impl == "reference":
+        return reference_arm(args, length, Hq, Hkv, D, dtype, cfg)
+
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if Hkv % world:
+        raise SystemExit("KV heads must divide evenly over the GPUs")
+    hkv_r = Hkv // world
+    G = Hq // Hkv
+    q, k, v = topic_qkv(length=length, query_heads=Hq, kv_heads=Hkv, head_dim=D, seed=0, dtype=dtype)
+    qs = q[rank * hkv_r * G:(rank + 1) * hkv_r * G].contiguous()
+    ks = k[rank * hkv_r:(rank + 1) * hkv_r].contiguous()
+    vs = v[rank * hkv_r:(rank + 1) * hkv_r].contiguous()
+    qd, kd, vd = qs.to(dev)[None], ks.to(dev)[None], vs.to(dev)[None]
+    out_full = torch.empty((world, hkv_r * G, length, D), dtype=dtype, device=dev) if world > 1 else None
+
+    def step():
+        out = fpv2.fpv2_sdpa(qd, kd, vd, scale=scale, config=base_cfg)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(out_full.view(-1), out[0].contiguous().view(-1))
+        return out
+
+    # Lists once, for the retained-FLOP count of this rank's shard.
+    pk, pv, lists, _ = fpv2.index_stage(qd[0], kd[0], vd[0], scale=scale, config=cfg, offset=0,
+                                        query_length=length, key_length=length)
+    flops_rank = retained_attention_flops(lists[0], lists[1], lists[3], G=G, tile_q=cfg.tile_q,
+                                          block_k=cfg.block_k, offset=0, valid_lq=length,
+                                          valid_lk=length, D=D, corr=cfg.mean_correction)
+    sel_total = int(lists[1].sum().item())
+    nt, nb = length // cfg.tile_q, length // cfg.block_k
+    visible = sum((min(t * cfg.tile_q + cfg.tile_q, length) - 1) // cfg.block_k + 1
+                  for t in range(nt)) * hkv_r
+    del pk, pv, lists
+    flops_total = torch.tensor([flops_rank], dtype=torch.float64, device=dev)
+    counts = torch.tensor([sel_total, visible], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(flops_total)
+        dist.all_reduce(counts)
+    flops_layer = float(flops_total.item())
+    sparsity = 1.0 - float(counts[0].item()) / float(counts[1].item())
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps, per-stage CUDA events on the launch stream ----
+    stream = torch.cuda.current_stream(dev)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    from fpv2.kernel import index_stage, sparse_attention
+
+    def step_timed(e):
+        e[0].record(stream)
+        pk_, pv_, lists_, _ = index_stage(qd[0], kd[0], vd[0], scale=scale, config=cfg, offset=0,
+                                          query_length=length, key_length=length)
+        e[1].record(stream)
+        out = sparse_attention(qd[0], kd[0], vd[0], pk_, pv_, *lists_, scale=scale, config=cfg,
+                               offset=0, query_length=length, key_length=length)
+        e[2].record(stream)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(out_full.view(-1), out.view(-1))
+        e[3].record(stream)
+
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for i in range(args.steps):
+            step_timed(ev[i])
+        end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    total_ms = start.elapsed_time(end)
+    idx_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    attn_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    gather_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in ev)
+    t = torch.tensor([total_ms, idx_ms, attn_ms, gather_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, idx_ms, attn_ms, gather_ms = [float(x) for x in t.tolist()]
+    ms_per_step = total_ms / args.steps
+
+    # ---- end-to-end through the public API with host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        qh = qs[None].pin_memory()
+        kh = ks[None].pin_memory()
+        vh = vs[None].pin_memory()
+        oh = torch.empty((1, hkv_r * G, length, D), dtype=dtype).pin_memory()
+        qb = torch.empty_like(qd)
+        kb = torch.empty_like(kd)
+        vb = torch.empty_like(vd)
+
+        def e2e_step():
+            qb.copy_(qh, non_blocking=True)
+            kb.copy_(kh, non_blocking=True)
+            vb.copy_(vh, non_blocking=True)
+            out = fpv2.fpv2_sdpa(qb, kb, vb, scale=scale, config=base_cfg)
+            if world > 1:
+                import torch.distributed as dist
+
+                dist.all_gather_into_tensor(out_full.view(-1), out[0].contiguous().view(-1))
+            oh.copy_(out, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_e2e = max(2, min(args.steps, 5))
+        s2.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        e2.record(stream)
+        torch.cuda.synchronize()
+        te = torch.tensor([s2.elapsed_time(e2) / n_e2e], dtype=torch.float64, device=dev)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = float(te.item())
+        esz = torch.finfo(dtype).bits // 8
+        h2d = (qs.numel() + ks.numel() + vs.numel()) * esz * world
+        d2h = qs.numel() * esz * world
+        e2e = {"value": round(flops_layer / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+               "ms_per_layer": round(e2e_ms, 3), "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h)}
+
+    # ---- CPU baseline (rank 0, N = 1 only) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
+        dt, fl, desc = cpu_sample(q, k, v, cfg, tiles_per_step=args.cpu_tiles)
+        cpu = {"value": round(fl / dt / 1e12, 6), "unit": "TFLOP/s", "cores": os.cpu_count(),
+               "kind": "port", "sample": desc, "seconds": round(dt, 2)}
+
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        nt_all, nb_all = length // cfg.tile_q, length // cfg.block_k
+        idx_bytes_rank = index_stage_bytes(hkv_r * G, hkv_r, length, D, nt_all, nb_all)
+        attn_tflops = flops_rank / (attn_ms * 1e-3) / 1e12
+        idx_gbs = idx_bytes_rank / (idx_ms * 1e-3) / 1e9
+        peak_t = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+        dense_flops = 4.0 * D * Hq * length * (length + 1) / 2
+        value = flops_layer / (ms_per_step * 1e-3) / 1e12
+        line = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(3, args.warmup),
+            "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16" if dtype == torch.bfloat16 else "fp16",
+            "data": "synthetic topic-block generator (seed 0), inputs resident in HBM",
+            "config": {
+                "workload": f"{args.config}: FPV2 layer L={length}, Hq={Hq}, Hkv={Hkv}, head_dim={D}, "
+                            f"alpha={alpha}, correction={'on' if cfg.mean_correction else 'off'}, "
+                            f"sink_tokens={cfg.sink_tokens}, window_tokens={cfg.window_tokens}, "
+                            f"last_n_blocks={cfg.last_n_blocks}, tile_q={cfg.tile_q} (128 packed rows)",
+                "parallelism": f"head-parallel x{world} (+NCCL all-gather of the output)" if world > 1
+                               else "single GPU",
+                "l2": "inputs (Q+K+V) larger than the 126 MB L2 at every step",
+                "ms_per_layer": round(ms_per_step, 4),
+                "index_stage_ms": round(idx_ms, 4),
+                "attention_ms": round(attn_ms, 4),
+                "allgather_ms": round(gather_ms, 4) if world > 1 else 0.0,
+                "retained_tflop_per_layer": round(flops_layer / 1e12, 4),
+                "dense_causal_tflop_per_layer": round(dense_flops / 1e12, 3),
+                "block_sparsity": round(sparsity, 4),
+                "selection_gbs": round(idx_gbs, 1),
+                "attention_tflops": round(attn_tflops, 1),
+                "attention_pct_bf16_peak": round(100 * attn_tflops / peak_t, 2),
+                "attention_pct_bf16_spec_2250": round(100 * attn_tflops / 2250.0, 2),
+                "selection_pct_hbm": round(100 * idx_gbs / peaks["hbm_gbs"], 2),
+            },
+            "roofline": {
+                "bound": "tensor", "kernel": "attn_tc_kernel (sparse attention)",
+                "achieved": round(attn_tflops, 1), "peak": peak_t, "unit": "TFLOP/s",
+                "frac": round(attn_tflops / peak_t, 4), "traffic": None,
+                "peak_source": f"{peak_src} bf16_tflops_sustained",
+            },
+            "roofline_index_stage": {
+                "bound": "hbm", "kernel": "pool_vec_kernel + select_tc_kernel",
+                "achieved": round(idx_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(idx_gbs / peaks["hbm_gbs"], 4), "traffic": None,
+                "algorithmic_bytes": idx_bytes_rank, "peak_source": f"{peak_src} hbm_gbs",
+            },
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": 3 * args.steps,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def reference_arm(args, length, Hq, Hkv, D, dtype, cfg) -> int:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from tests.synthetic import topic_qkv
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    q, k, v = topic_qkv(length=length, query_heads=Hq, kv_heads=Hkv, head_dim=D, seed=0, dtype=dtype)
+    for _ in range(max(3, args.warmup)):
+        cpu_sample(q, k, v, cfg, tiles_per_step=max(8, args.cpu_tiles // 8))
+    times, flops, desc = [], [], ""
+    for _ in range(args.steps):
+        dt, fl, desc = cpu_sample(q, k, v, cfg, tiles_per_step=max(8, args.cpu_tiles // 8))
+        times.append(dt)
+        flops.append(fl)
+    value = sum(flops) / sum(times) / 1e12
+    ms = 1e3 * sum(times) / len(times)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": max(3, args.warmup),
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16" if dtype == torch.bfloat16 else "fp16",
+        "data": "synthetic topic-block generator (seed 0)",
+        "config": {"workload": f"{args.config}: FPV2 layer L={length}, Hq={Hq}, Hkv={Hkv}, head_dim={D}, "
+                               f"alpha={cfg.alpha}, correction={'on' if cfg.mean_correction else 'off'}; "
+                               "CPU port of the reference algorithm on a bounded sample per step"},
+        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": os.cpu_count(),
+                         "kind": "port", "sample": desc},
+        "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,627 @@
+// Block-sparse attention on tensor cores (tcgen05 + TMEM + TMA).
+//
+// Math (fpv2/kernel.py:187-414): for each query row, an online softmax in
+// base 2 over the keys of the selected blocks (causal / key_length masked,
+// masked logits = finite_min), followed by the pruned blocks as pooled K/V
+// entries whose logits are shifted by log2(block_k); out = O / l.
+//
+// A work item is one 128-row chunk of a selection tile: the G query heads of
+// one KV head packed together (GQA packing), so every K/V tile loaded feeds
+// all G heads. Per KV item (one 128-key sub-tile of a selected block, or one
+// chunk of up to 128 pooled entries):
+//   S[128x128] = Q . K^T          tcgen05.mma SS, fp32 in TMEM (double buffered)
+//   P = 2^(S*c - m)               softmax warps: TMEM -> regs -> bf16/f16 P back
+//                                 into the same TMEM columns
+//   O[128xD] += P . V             tcgen05.mma TS (A = P from TMEM, B = V MN-major)
+// The running max is rescaled lazily: O in TMEM is only rescaled when a row's
+// max grows by more than 2^8, which leaves the final O/l unchanged.
+//
+// Warp roles (192 threads, one persistent CTA per SM):
+//   warp 0     producer: walks the lists, publishes one record per KV item,
+//              TMA-loads Q / K / V tiles (128B swizzle) and gathers pooled
+//              K/V rows for correction items with plain loads (no multicast);
+//   warp 1     MMA issuer;
+//   warps 2-5  softmax (thread = query row) and the output epilogue.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace fpv2 {
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kStages = 2;      // K/V tiles and S buffers
+constexpr int kRecs = 8;        // item records in flight
+constexpr int kTmemCols = 512;
+constexpr float kRescaleThreshold = 8.0f;   // log2 units
+
+enum : int { KIND_SEL = 0, KIND_CORR = 1, KIND_EMPTY = 2 };
+
+struct Rec {
+  int kind;
+  int kstart;   // SEL: first key; CORR: first list entry
+  int nvalid;   // CORR: valid entries in this chunk
+  int last;     // last item of the work item
+};
+
+template <int D>
+struct Cfg {
+  static constexpr int kHalves = D / 64;
+  static constexpr int kTileBytes = 128 * D * 2;   // Q, K or V tile
+  static constexpr int kOCol = 0;                  // O accumulator columns [0, D)
+  static constexpr int kSCol = D;                  // S buffers at D, D + 128
+};
+
+struct Params {
+  AttnArgs a;
+  int nch;          // 128-row chunks per tile
+  int items;        // total work items
+  uint32_t idesc_qk, idesc_pv;
+  int* status;
+  long long budget;
+};
+
+struct Chunk {
+  int h, t, c;
+  int g0, p0;               // first head / position of the chunk inside the tile
+  long long abs_last;       // last valid absolute query position of the chunk
+};
+
+__device__ __forceinline__ Chunk make_chunk(const Params& p, int w) {
+  const AttnArgs& a = p.a;
+  Chunk ck;
+  const int per_t = a.Hkv * p.nch;
+  ck.t = a.Nt - 1 - w / per_t;
+  const int r = w % per_t;
+  ck.h = r / p.nch;
+  ck.c = r % p.nch;
+  const int P0 = ck.c * 128;
+  ck.g0 = P0 / a.tile_q;
+  ck.p0 = P0 % a.tile_q;
+  const long long span = min(a.tile_q, 128);
+  const long long last_row = min((long long)ck.t * a.tile_q + ck.p0 + span, (long long)a.valid_lq) - 1;
+  ck.abs_last = (long long)a.offset + last_row;
+  return ck;
+}
+
+__device__ __forceinline__ int clampi(int x, int lo, int hi) { return min(max(x, lo), hi); }
+
+template <int D, int DT>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                   const __grid_constant__ CUtensorMap tmap_k,
+                   const __grid_constant__ CUtensorMap tmap_v, Params p) {
+  using C = Cfg<D>;
+  const AttnArgs& a = p.a;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw_base);
+
+  const uint32_t q_smem = base;                                   // [2][tile]
+  const uint32_t k_smem = base + 2 * C::kTileBytes;               // [kStages][tile]
+  const uint32_t v_smem = k_smem + kStages * C::kTileBytes;       // [kStages][tile]
+  uint8_t* after_tiles = gbase + (2 + 2 * kStages) * C::kTileBytes;
+  Rec* recs = reinterpret_cast<Rec*>(after_tiles);                // [kRecs]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(recs + kRecs);
+  uint64_t* q_full = bars;              // [2]
+  uint64_t* q_empty = q_full + 2;       // [2]
+  uint64_t* rec_full = q_empty + 2;     // [kRecs]
+  uint64_t* rec_empty = rec_full + kRecs;
+  uint64_t* k_full = rec_empty + kRecs; // [kStages]
+  uint64_t* k_empty = k_full + kStages;
+  uint64_t* v_full = k_empty + kStages;
+  uint64_t* v_empty = v_full + kStages;
+  uint64_t* s_full = v_empty + kStages;
+  uint64_t* s_free = s_full + kStages;
+  uint64_t* p_full = s_free + kStages;
+  uint64_t* pv_done = p_full + kStages;  // [1]
+  uint64_t* o_full = pv_done + 1;        // [1]
+  uint64_t* o_free = o_full + 1;         // [1]
+  uint64_t* drain = o_free + 1;          // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&q_full[i]), 1);
+      mbar_init(smem_u32(&q_empty[i]), 1);
+    }
+    for (int i = 0; i < kRecs; ++i) {
+      mbar_init(smem_u32(&rec_full[i]), 1);
+      mbar_init(smem_u32(&rec_empty[i]), 1 + 4);   // MMA thread + 4 softmax warps
+    }
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(smem_u32(&k_full[i]), 1);
+      mbar_init(smem_u32(&k_empty[i]), 1);
+      mbar_init(smem_u32(&v_full[i]), 1);
+      mbar_init(smem_u32(&v_empty[i]), 1);
+      mbar_init(smem_u32(&s_full[i]), 1);
+      mbar_init(smem_u32(&s_free[i]), 1);
+      mbar_init(smem_u32(&p_full[i]), 4);
+    }
+    mbar_init(smem_u32(pv_done), 1);
+    mbar_init(smem_u32(o_full), 1);
+    mbar_init(smem_u32(o_free), 4);
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_q);
+    tma_prefetch_desc(&tmap_k);
+    tma_prefetch_desc(&tmap_v);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  WaitCtx wc{p.status, abort_flag, p.budget};
+  const int bk_sub = a.block_k / 128;
+
+  if (warp == 0) {
+    // ============================ producer ================================
+    int qcount = 0, icount = 0, kv = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x) {
+      const Chunk ck = make_chunk(p, w);
+      const long long lrow = ((long long)ck.h * a.Nt + ck.t) * a.Nb;
+      const int nsel = clampi(a.sel_counts[(long long)ck.h * a.Nt + ck.t], 0, a.Nb);
+      const int npr = a.corr ? clampi(a.pr_counts[(long long)ck.h * a.Nt + ck.t], 0, a.Nb) : 0;
+      // Q tile of the chunk.
+      {
+        const int qs = qcount & 1;
+        if (lane == 0) ok = mbar_wait(smem_u32(&q_empty[qs]), ((qcount >> 1) & 1) ^ 1, wc);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        if (lane == 0) {
+          const uint32_t qb = smem_u32(&q_full[qs]);
+          mbar_arrive_expect_tx(qb, (uint32_t)C::kTileBytes);
+#pragma unroll
+          for (int hh = 0; hh < C::kHalves; ++hh)
+            tma_load_3d(q_smem + qs * C::kTileBytes + hh * 16384, &tmap_q, qb, hh * 64,
+                        ck.t * a.tile_q + ck.p0, ck.h * a.G + ck.g0);
+        }
+        ++qcount;
+      }
+      // Count the KV items (the walk stops at the first block past the chunk,
+      // fpv2/kernel.py:249-255).
+      int n_sel_items = 0, brk = nsel;
+      for (int i0 = 0; i0 < nsel; i0 += 32) {
+        const int i = i0 + lane;
+        const bool in = i < nsel;
+        const int blk = in ? clampi(a.sel_ids[lrow + i], 0, a.Nb - 1) : 0;
+        const long long bstart = (long long)blk * a.block_k;
+        const unsigned stop = __ballot_sync(0xffffffffu, in && bstart > ck.abs_last);
+        const int lim = stop ? (__ffs(stop) - 1) : 32;
+        int contrib = 0;
+        if (in && lane < lim) contrib = (int)min((long long)bk_sub, (ck.abs_last - bstart) / 128 + 1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) contrib += __shfl_xor_sync(0xffffffffu, contrib, o);
+        n_sel_items += contrib;
+        if (stop) { brk = i0 + lim; break; }
+      }
+      const int n_corr_items = (npr + 127) / 128;
+      const int n_items = max(1, n_sel_items + n_corr_items);
+      int emitted = 0;
+
+      // Publish one record (and its K/V data) per item.
+      auto emit = [&](int kind, int kstart, int nvalid) -> bool {
+        const int ri = icount % kRecs;
+        bool good = true;
+        if (lane == 0) good = mbar_wait(smem_u32(&rec_empty[ri]), ((icount / kRecs) & 1) ^ 1, wc);
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) return false;
+        if (lane == 0) {
+          recs[ri].kind = kind;
+          recs[ri].kstart = kstart;
+          recs[ri].nvalid = nvalid;
+          recs[ri].last = (emitted == n_items - 1) ? 1 : 0;
+          mbar_arrive(smem_u32(&rec_full[ri]));
+        }
+        ++icount;
+        ++emitted;
+        if (kind == KIND_EMPTY) return true;
+        const int st = kv % kStages;
+        const uint32_t par = ((kv / kStages) & 1) ^ 1;
+        if (lane == 0) {
+          good = mbar_wait(smem_u32(&k_empty[st]), par, wc);
+          if (good) good = mbar_wait(smem_u32(&v_empty[st]), par, wc);
+        }
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) return false;
+        const uint32_t kst = k_smem + st * C::kTileBytes;
+        const uint32_t vst = v_smem + st * C::kTileBytes;
+        if (kind == KIND_SEL) {
+          if (lane == 0) {
+            const uint32_t kb = smem_u32(&k_full[st]);
+            mbar_arrive_expect_tx(kb, (uint32_t)C::kTileBytes);
+#pragma unroll
+            for (int hh = 0; hh < C::kHalves; ++hh)
+              tma_load_3d(kst + hh * 16384, &tmap_k, kb, hh * 64, kstart, ck.h);
+            const uint32_t vb = smem_u32(&v_full[st]);
+            mbar_arrive_expect_tx(vb, (uint32_t)C::kTileBytes);
+#pragma unroll
+            for (int hh = 0; hh < C::kHalves; ++hh)
+              tma_load_3d(vst + hh * 16384, &tmap_v, vb, hh * 64, kstart, ck.h);
+          }
+        } else {
+          // Gather pooled rows into the swizzled K and V tiles.
+          constexpr int kChunks = D / 8;   // 16-byte chunks per row
+          for (int idx = lane; idx < 128 * kChunks; idx += 32) {
+            const int e = idx / kChunks, cidx = idx % kChunks;
+            const int hh = cidx >> 3, cc = cidx & 7;
+            const uint32_t off = hh * 16384 + e * 128 + ((cc ^ (e & 7)) << 4);
+            uint4 kvk = make_uint4(0, 0, 0, 0), kvv = make_uint4(0, 0, 0, 0);
+            if (e < nvalid) {
+              const int blk = clampi(a.pr_ids[lrow + kstart + e], 0, a.Nb - 1);
+              const long long src = ((long long)ck.h * a.Nb + blk) * D + cidx * 8;
+              if (a.pooled_dt == DT) {
+                kvk = __ldg(reinterpret_cast<const uint4*>(
+                    reinterpret_cast<const typename Elem<DT>::T*>(a.pk) + src));
+                kvv = __ldg(reinterpret_cast<const uint4*>(
+                    reinterpret_cast<const typename Elem<DT>::T*>(a.pv) + src));
+              } else {   // float32 pooled: round to the compute dtype
+                const float4* fk = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.pk) + src);
+                const float4* fv = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.pv) + src);
+                const float4 k0 = __ldg(fk), k1 = __ldg(fk + 1), v0 = __ldg(fv), v1 = __ldg(fv + 1);
+                kvk = make_uint4(pack2<DT>(k0.x, k0.y), pack2<DT>(k0.z, k0.w), pack2<DT>(k1.x, k1.y),
+                                 pack2<DT>(k1.z, k1.w));
+                kvv = make_uint4(pack2<DT>(v0.x, v0.y), pack2<DT>(v0.z, v0.w), pack2<DT>(v1.x, v1.y),
+                                 pack2<DT>(v1.z, v1.w));
+              }
+            }
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(kst + off), "r"(kvk.x),
+                         "r"(kvk.y), "r"(kvk.z), "r"(kvk.w)
+                         : "memory");
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(vst + off), "r"(kvv.x),
+                         "r"(kvv.y), "r"(kvv.z), "r"(kvv.w)
+                         : "memory");
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(smem_u32(&k_full[st]));
+            mbar_arrive(smem_u32(&v_full[st]));
+          }
+        }
+        ++kv;
+        return true;
+      };
+
+      for (int i0 = 0; i0 < brk && ok; i0 += 32) {
+        const int i = i0 + lane;
+        const int blk = i < brk ? clampi(a.sel_ids[lrow + i], 0, a.Nb - 1) : 0;
+        const int cnt = min(32, brk - i0);
+        for (int j = 0; j < cnt && ok; ++j) {
+          const int bj = __shfl_sync(0xffffffffu, blk, j);
+          const long long bstart = (long long)bj * a.block_k;
+          for (int sub = 0; sub < bk_sub && ok; ++sub) {
+            const long long ks = bstart + sub * 128;
+            if (ks > ck.abs_last) break;
+            ok = emit(KIND_SEL, (int)ks, 0);
+          }
+        }
+      }
+      for (int j = 0; j < n_corr_items && ok; ++j)
+        ok = emit(KIND_CORR, j * 128, min(128, npr - j * 128));
+      if (ok && n_sel_items + n_corr_items == 0) ok = emit(KIND_EMPTY, 0, 0);
+    }
+    // Drain in-flight bulk copies before the CTA retires.
+    if (lane == 0) {
+      for (int i = 0; i < kStages; ++i) {
+        const int uses = (kv - i + kStages - 1) / kStages;
+        if (uses > 0) {
+          mbar_wait(smem_u32(&k_full[i]), (uses - 1) & 1, wc, false);
+          mbar_wait(smem_u32(&v_full[i]), (uses - 1) & 1, wc, false);
+        }
+      }
+      for (int i = 0; i < 2; ++i) {
+        const int uses = (qcount - i + 1) / 2;
+        if (uses > 0) mbar_wait(smem_u32(&q_full[i]), (uses - 1) & 1, wc, false);
+      }
+    }
+  } else if (warp == 1) {
+    // ============================ MMA issuer ==============================
+    if (lane == 0) {
+      int qcount = 0, icount = 0, kv = 0, wi = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++wi) {
+        const int qs = qcount & 1;
+        ok = mbar_wait(smem_u32(&q_full[qs]), (qcount >> 1) & 1, wc);
+        if (!ok) break;
+        ++qcount;
+        bool need_ofree = wi > 0;
+        bool first_pv = true;
+        int prev = -1;   // kv index whose PV is pending
+        auto issue_pv = [&](int n) -> bool {
+          const int st = n % kStages;
+          const uint32_t par = (n / kStages) & 1;
+          if (!mbar_wait(smem_u32(&p_full[st]), par, wc)) return false;
+          if (!mbar_wait(smem_u32(&v_full[st]), par, wc)) return false;
+          if (need_ofree) {
+            if (!mbar_wait(smem_u32(o_free), (wi - 1) & 1, wc)) return false;
+            need_ofree = false;
+          }
+          tc_fence_after();
+          const uint32_t o_tmem = tmem_base + C::kOCol;
+          const uint32_t p_tmem = tmem_base + C::kSCol + st * 128;
+          const uint32_t vst = v_smem + st * C::kTileBytes;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t bdesc = sw128_desc(vst + kk * 2048, 16384, 1024);
+            umma_ts(o_tmem, p_tmem + kk * 8, bdesc, p.idesc_pv, (first_pv && kk == 0) ? 0u : 1u);
+          }
+          first_pv = false;
+          umma_commit(smem_u32(&v_empty[st]));
+          umma_commit(smem_u32(&s_free[st]));
+          umma_commit(smem_u32(pv_done));
+          return true;
+        };
+        while (ok) {
+          const int ri = icount % kRecs;
+          ok = mbar_wait(smem_u32(&rec_full[ri]), (icount / kRecs) & 1, wc);
+          if (!ok) break;
+          const Rec rec = recs[ri];
+          mbar_arrive(smem_u32(&rec_empty[ri]));
+          ++icount;
+          if (rec.kind != KIND_EMPTY) {
+            const int st = kv % kStages;
+            const uint32_t par = (kv / kStages) & 1;
+            ok = mbar_wait(smem_u32(&k_full[st]), par, wc);
+            if (ok) ok = mbar_wait(smem_u32(&s_free[st]), par ^ 1, wc);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t s_tmem = tmem_base + C::kSCol + st * 128;
+            const uint32_t qb = q_smem + qs * C::kTileBytes;
+            const uint32_t kb = k_smem + st * C::kTileBytes;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const int hh = kk / 4, sub = kk % 4;
+              const uint64_t adesc = sw128_desc(qb + hh * 16384 + sub * 32, 16, 1024);
+              const uint64_t bdesc = sw128_desc(kb + hh * 16384 + sub * 32, 16, 1024);
+              umma_ss(s_tmem, adesc, bdesc, p.idesc_qk, kk > 0 ? 1u : 0u);
+            }
+            umma_commit(smem_u32(&s_full[st]));
+            umma_commit(smem_u32(&k_empty[st]));
+            if (prev >= 0) ok = issue_pv(prev);
+            prev = kv;
+            ++kv;
+          }
+          if (rec.last) break;
+        }
+        if (ok && prev >= 0) ok = issue_pv(prev);
+        if (!ok) break;
+        umma_commit(smem_u32(&q_empty[qs]));
+        if (need_ofree) {
+          ok = mbar_wait(smem_u32(o_free), (wi - 1) & 1, wc);
+          need_ofree = false;
+        }
+        umma_commit(smem_u32(o_full));
+      }
+      umma_commit(smem_u32(drain));
+      mbar_wait(smem_u32(drain), 0, wc, false);
+    }
+  } else {
+    // ======================= softmax + epilogue ============================
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;          // row of the 128-row chunk
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float c2 = a.scale_log2;
+    int icount = 0, kv = 0, wi = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++wi) {
+      const Chunk ck = make_chunk(p, w);
+      const int P = ck.c * 128 + r;
+      const int gq = P / a.tile_q;
+      const int pos = P % a.tile_q;
+      const long long row = (long long)ck.t * a.tile_q + pos;
+      const long long position = (long long)a.offset + row;
+      const bool row_valid = row < a.valid_lq;
+      float m_used = kFiniteMin, l = 0.f;
+      int pv_wi = 0;
+      while (true) {
+        const int ri = icount % kRecs;
+        ok = mbar_wait(smem_u32(&rec_full[ri]), (icount / kRecs) & 1, wc);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        const Rec rec = recs[ri];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&rec_empty[ri]));
+        ++icount;
+        if (rec.kind == KIND_EMPTY) break;
+        const int st = kv % kStages;
+        const uint32_t par = (kv / kStages) & 1;
+        ok = mbar_wait(smem_u32(&s_full[st]), par, wc);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t s_tmem = tmem_base + lane_off + C::kSCol + st * 128;
+        uint32_t s[4][32];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(s_tmem + q4 * 32, s[q4]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) reg_fence(s[q4]);
+        float x[4][32];
+        float mt = kFiniteMin;
+        if (rec.kind == KIND_SEL) {
+          const long long ks = rec.kstart;
+          const bool full = row_valid && ks + 127 <= position && ks + 127 < a.valid_lk;
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const long long key = ks + q4 * 32 + j;
+              const bool v = full || (row_valid && key <= position && key < a.valid_lk);
+              x[q4][j] = v ? __uint_as_float(s[q4][j]) * c2 : kFiniteMin;
+              mt = fmaxf(mt, x[q4][j]);
+            }
+        } else {
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const bool v = q4 * 32 + j < rec.nvalid;
+              x[q4][j] = v ? fmaf(__uint_as_float(s[q4][j]), c2, a.corr_shift) : kFiniteMin;
+              mt = fmaxf(mt, x[q4][j]);
+            }
+        }
+        const float m_new = fmaxf(m_used, mt);
+        const bool need = m_new > m_used + kRescaleThreshold ||
+                          (m_used == kFiniteMin && m_new > kFiniteMin);
+        if (__any_sync(0xffffffffu, need)) {
+          const float f = need ? ex2(m_used - m_new) : 1.f;
+          if (need) {
+            m_used = m_new;
+            l *= f;
+          }
+          if (pv_wi > 0) {
+            // O holds PVs of this work item: wait for the latest one, rescale rows.
+            ok = mbar_wait(smem_u32(pv_done), (kv - 1) & 1, wc);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc_fence_after();
+#pragma unroll
+            for (int dc = 0; dc < D / 32; ++dc) {
+              uint32_t o[32];
+              const uint32_t oaddr = tmem_base + lane_off + C::kOCol + dc * 32;
+              tmem_ld32(oaddr, o);
+              tmem_wait_ld();
+              reg_fence(o);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * f);
+              tmem_st32(oaddr, o);
+            }
+            tmem_wait_st();
+          }
+        }
+        float rs = 0.f;
+        uint32_t pk[2][32];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const float p0 = ex2(x[q4][j] - m_used);
+            const float p1 = ex2(x[q4][j + 1] - m_used);
+            rs += p0 + p1;
+            pk[q4 >> 1][(q4 & 1) * 16 + (j >> 1)] = pack2<DT>(p0, p1);
+          }
+        l += rs;
+        tmem_st32(s_tmem, pk[0]);
+        tmem_st32(s_tmem + 32, pk[1]);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&p_full[st]));
+        ++kv;
+        ++pv_wi;
+        if (rec.last) break;
+      }
+      if (!ok) break;
+      // ---- epilogue: O / l -> out ------------------------------------------
+      ok = mbar_wait(smem_u32(o_full), wi & 1, wc);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      using T = typename Elem<DT>::T;
+      T* out = reinterpret_cast<T*>(a.out) +
+               (((long long)(ck.h * a.G + gq)) * a.Lq_pad + row) * D;
+      const float inv = pv_wi > 0 ? 1.f / l : 0.f;
+#pragma unroll
+      for (int dc = 0; dc < D / 32; ++dc) {
+        uint32_t o[32];
+        if (pv_wi > 0) {
+          tmem_ld32(tmem_base + lane_off + C::kOCol + dc * 32, o);
+          tmem_wait_ld();
+          reg_fence(o);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] = 0u;
+        }
+        uint32_t packed[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          packed[j] = pack2<DT>(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
+        uint4* dst = reinterpret_cast<uint4*>(out + dc * 32);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(o_free));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+}
+
+template <int D>
+size_t smem_bytes() {
+  return 1024 + (size_t)(2 + 2 * kStages) * Cfg<D>::kTileBytes + sizeof(Rec) * kRecs +
+         8 * (4 + 2 * kRecs + 7 * kStages + 4) + 16;
+}
+
+}  // namespace
+
+bool attn_tc_supported(const AttnArgs& a) {
+  if (a.dt != DT_BF16 && a.dt != DT_F16) return false;
+  if (a.D != 64 && a.D != 128) return false;
+  if (a.pooled_dt != a.dt && a.pooled_dt != DT_F32) return false;
+  if (a.block_k % 128 != 0) return false;
+  const int R = a.G * a.tile_q;
+  if (R % 128 != 0) return false;
+  if (a.tile_q % 128 != 0 && 128 % a.tile_q != 0) return false;
+  return true;
+}
+
+cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, cudaStream_t stream) {
+  Params p;
+  p.a = a;
+  p.nch = (a.G * a.tile_q) / 128;
+  p.items = a.Hkv * a.Nt * p.nch;
+  const int fmt = a.dt == DT_BF16 ? 1 : 0;
+  p.idesc_qk = umma_idesc_f16(fmt, 128, 128, 0, 0);
+  p.idesc_pv = umma_idesc_f16(fmt, 128, a.D, 0, 1);
+  p.status = L.status;
+  p.budget = L.budget;
+  if (p.items == 0) return cudaSuccess;
+
+  const int box_rows = a.tile_q >= 128 ? 128 : a.tile_q;
+  const int box_heads = 128 / box_rows;
+  CUtensorMap tq, tk, tv;
+  if (!encode_tmap_3d(&tq, a.q, a.dt, a.D, a.Lq_pad, a.Hq, 64, box_rows, box_heads))
+    return cudaErrorInvalidValue;
+  if (!encode_tmap_3d(&tk, a.k, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return cudaErrorInvalidValue;
+  if (!encode_tmap_3d(&tv, a.v, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return cudaErrorInvalidValue;
+  const int grid = max(1, min(L.num_sms, p.items));
+  cudaError_t e = cudaSuccess;
+#define FPV2_ATTN_LAUNCH(DD, TT)                                                            \
+  {                                                                                         \
+    const size_t smem = smem_bytes<DD>();                                                   \
+    e = cudaFuncSetAttribute(attn_tc_kernel<DD, TT>,                                        \
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
+    if (e != cudaSuccess) return e;                                                         \
+    attn_tc_kernel<DD, TT><<<grid, kThreads, smem, stream>>>(tq, tk, tv, p);                \
+  }
+  if (a.D == 64 && a.dt == DT_BF16) FPV2_ATTN_LAUNCH(64, DT_BF16)
+  else if (a.D == 64 && a.dt == DT_F16) FPV2_ATTN_LAUNCH(64, DT_F16)
+  else if (a.D == 128 && a.dt == DT_BF16) FPV2_ATTN_LAUNCH(128, DT_BF16)
+  else if (a.D == 128 && a.dt == DT_F16) FPV2_ATTN_LAUNCH(128, DT_F16)
+  else return cudaErrorInvalidValue;
+#undef FPV2_ATTN_LAUNCH
+  return cudaGetLastError();
+}
+
+}  // namespace fpv2

@@ -1,0 +1,105 @@
+// Launcher interfaces between the C-ABI layer (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fpv2 {
+
+// ---- pooling (pool.cu) ----------------------------------------------------
+struct PoolArgs {
+  const void* x[2];
+  void* out[2];
+  int64_t heads, length;
+  int D, bs;
+};
+cudaError_t launch_pool(const PoolArgs& a, int ntensors, int dt_in, int dt_out,
+                        cudaStream_t stream);
+
+// ---- selection geometry shared by all selection kernels -----------------
+struct SelectGeom {
+  int Hq, Hkv, G, Lq_pad, Nb, D, Nt;
+  int offset, valid_lq, valid_lk;
+  int block_k, tile_q, sink, window, last_n;
+  float scale, alpha;
+};
+
+// Padded lists written by the selection kernels (all null = not written).
+struct SelectLists {
+  int32_t* sel_ids;
+  int32_t* sel_counts;
+  int32_t* pr_ids;
+  int32_t* pr_counts;
+};
+
+// ---- generic (CUDA-core) kernels (generic.cu) ------------------------------
+// Mask (nullable) and lists (nullable) for every (kv head, tile); any dtype of
+// q / pooled_k, any head_dim.
+cudaError_t launch_select_generic(const SelectGeom& g, const void* q, int q_dt, const void* pk,
+                                  int pk_dt, uint8_t* mask, const SelectLists& lists,
+                                  cudaStream_t stream);
+// Unmasked scale * q . pooled_k for every row and block.
+cudaError_t launch_raw_scores(const SelectGeom& g, const void* q, int q_dt, const void* pk,
+                              int pk_dt, float* out, cudaStream_t stream);
+// Mask -> lists.
+cudaError_t launch_compact(const uint8_t* mask, int Hkv, int Nt, int Nb, int block_k, int tile_q,
+                           int offset, int valid_lk, int32_t* sel_ids, int32_t* sel_counts,
+                           int32_t* pr_ids, int32_t* pr_counts, cudaStream_t stream);
+
+struct AttnArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* pk;
+  const void* pv;
+  int pooled_dt;
+  const int32_t* sel_ids;
+  const int32_t* sel_counts;
+  const int32_t* pr_ids;
+  const int32_t* pr_counts;
+  void* out;
+  int dt;
+  int Hq, Hkv, G, Lq_pad, Lk_pad, D, Nt, Nb;
+  int offset, valid_lq, valid_lk, block_k, tile_q, corr;
+  float scale_log2;   // scale * log2(e)
+  float corr_shift;   // log2(block_k)
+};
+cudaError_t launch_attn_generic(const AttnArgs& a, cudaStream_t stream);
+
+// ---- tcgen05 kernels -------------------------------------------------------
+struct TcLaunch {
+  int* status;
+  long long budget;
+  int num_sms;
+};
+
+// select_tc.cu: fused score + energy + threshold + lists on tensor cores.
+struct SelectTcArgs {
+  SelectGeom g;
+  int NC;               // query rows per MMA N-chunk (R if R < 128, else 128)
+  int box_rows;         // TMA box rows (positions) of one Q chunk
+  int box_heads;        // TMA box heads of one Q chunk
+  int dt;               // DT_F16 / DT_BF16 (q and pooled_k)
+  uint8_t* mask;        // nullable
+  int32_t* sel_ids;     // nullable (lists not written)
+  int32_t* sel_counts;
+  int32_t* pr_ids;
+  int32_t* pr_counts;
+};
+bool select_tc_supported(const SelectGeom& g, int dt);
+cudaError_t launch_select_tc(const SelectTcArgs& a, const void* q, const void* pk,
+                             const TcLaunch& L, cudaStream_t stream);
+
+// attn_tc.cu: FlashAttention-style block-sparse attention on tensor cores.
+bool attn_tc_supported(const AttnArgs& a);
+cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, cudaStream_t stream);
+
+// selftest.cu: bounded-wait failure detection.
+cudaError_t launch_wait_selftest(const TcLaunch& L, cudaStream_t stream);
+
+// tensor map helper (capi.cu)
+bool encode_tmap_3d(CUtensorMap* map, const void* base, int dt, uint64_t d0, uint64_t d1,
+                    uint64_t d2, uint32_t b0, uint32_t b1, uint32_t b2);
+
+}  // namespace fpv2

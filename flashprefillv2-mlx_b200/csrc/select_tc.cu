@@ -1,0 +1,496 @@
+// Index stage on tensor cores: scores, tile energies, alpha threshold,
+// forcing and list compaction for one (KV head, query tile) per work item.
+//
+// Math (fpv2/selection.py:144-195, fpv2/kernel.py:170-183):
+//   s[r, b]  = scale * q[r] . kbar[b]                 r over the tile's G*tile_q packed rows
+//   M        = max over visible rows r and fully visible blocks b of s[r, b]
+//   E[b]     = sum_r exp(s[r, b] - M)                 fully visible blocks only, else 0
+//   sel[b]   = E[b] >= alpha * max_b E[b]
+//   mask[b]  = (sel | sink | local | dense_tail) & visible
+// The tensor cores compute the transposed score tile S^T = Kbar . Q^T
+// (M = 128 blocks per TMEM lane group, N = the tile's packed query rows), so a
+// thread owns one block: its max m_b and sum e_b = sum_r 2^(x - m_b) (x = s*log2 e)
+// are register-local. The tile max is then M = max_b m_b and
+// E[b] = e_b * 2^(m_b - M): no cross-thread reduction touches the N*Nb scores.
+//
+// Warp roles (192 threads, one persistent CTA per SM):
+//   warp 0  TMA producer: Q chunks [N x D] and pooled-K tiles [128 x D], 128B swizzle.
+//           A pooled-K tile stays in its ring slot while the CTA keeps the same
+//           KV head, so pooled K is read from L2 once per CTA when Nb <= 128*slots.
+//   warp 1  MMA issuer (tcgen05.mma kind::f16, fp32 accumulators in TMEM).
+//   warps 2-5  energy + finalize: TMEM -> registers, masked max / exp2-sums,
+//           then threshold, forcing and ballot-based compaction into the
+//           full-width padded lists.
+// Work items are (kv head, tile) with tiles latest-first; CTA c keeps KV head
+// c % Hkv whenever the grid is a multiple of Hkv.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace fpv2 {
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr int kTmemSlots = 4;        // 128 columns each
+constexpr int kMaxNb = 2048;
+
+template <int D>
+struct Cfg {
+  static constexpr int kHalves = D / 64;
+  static constexpr int kQStages = 2;
+  static constexpr int kKStages = (D == 64) ? 8 : 4;
+  static constexpr int kQBytes = 128 * D * 2;   // up to 128 rows per chunk
+  static constexpr int kKBytes = 128 * D * 2;
+  static constexpr int kOpBytes = kQStages * kQBytes + kKStages * kKBytes;
+};
+
+struct Params {
+  SelectGeom g;
+  int NC, box_rows, n_chunks;
+  uint32_t idesc;
+  float scale_log2;
+  uint8_t* mask;
+  int32_t* sel_ids;
+  int32_t* sel_counts;
+  int32_t* pr_ids;
+  int32_t* pr_counts;
+  int* status;
+  long long budget;
+};
+
+struct Item {
+  int h, t;
+  long long tile_first, tile_last;
+  int n_full, n_mt;
+  bool row_mask;   // some (row, fully visible block) pair needs a per-element test
+};
+
+__device__ __forceinline__ Item make_item(const Params& p, int w) {
+  const SelectGeom& g = p.g;
+  Item it;
+  it.h = w % g.Hkv;
+  it.t = g.Nt - 1 - w / g.Hkv;
+  it.tile_first = (long long)g.offset + (long long)it.t * g.tile_q;
+  it.tile_last = min(it.tile_first + g.tile_q, (long long)g.offset + g.valid_lq) - 1;
+  it.n_full = 0;
+  if (it.tile_last + 1 >= g.block_k)
+    it.n_full = (int)min((long long)g.Nb, (it.tile_last + 1) / g.block_k);
+  it.n_mt = (it.n_full + 127) / 128;
+  const bool all_rows_valid = (long long)(it.t + 1) * g.tile_q <= g.valid_lq;
+  const bool all_see_all =
+      it.n_full == 0 || (long long)(it.n_full - 1) * g.block_k <= it.tile_first;
+  it.row_mask = !(all_rows_valid && all_see_all);
+  return it;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                     const __grid_constant__ CUtensorMap tmap_k, Params p) {
+  using C = Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw_base);
+  const SelectGeom& g = p.g;
+  const int Nb = g.Nb;
+  const int nwords = (Nb + 31) / 32;
+
+  // ---- shared memory carve-up -------------------------------------------
+  const uint32_t q_smem = base;
+  const uint32_t k_smem = base + C::kQStages * C::kQBytes;
+  float2* stats = reinterpret_cast<float2*>(gbase + C::kOpBytes);          // [Nb]
+  uint32_t* selw = reinterpret_cast<uint32_t*>(stats + Nb);               // [nwords]
+  uint32_t* prw = selw + nwords;
+  int* selpre = reinterpret_cast<int*>(prw + nwords);                     // [nwords]
+  int* prpre = selpre + nwords;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(prpre + nwords) + 7) & ~uintptr_t(7));
+  uint64_t* q_full = bars;
+  uint64_t* q_empty = q_full + C::kQStages;
+  uint64_t* k_full = q_empty + C::kQStages;
+  uint64_t* k_empty = k_full + C::kKStages;
+  uint64_t* t_full = k_empty + C::kKStages;
+  uint64_t* t_empty = t_full + kTmemSlots;
+  uint64_t* drain = t_empty + kTmemSlots;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* red = reinterpret_cast<float*>(tmem_slot + 2);   // [8]
+  int* totals = reinterpret_cast<int*>(red + 8);          // [2]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::kQStages; ++i) {
+      mbar_init(smem_u32(&q_full[i]), 1);
+      mbar_init(smem_u32(&q_empty[i]), 1);
+    }
+    for (int i = 0; i < C::kKStages; ++i) {
+      mbar_init(smem_u32(&k_full[i]), 1);
+      mbar_init(smem_u32(&k_empty[i]), 1);
+    }
+    for (int i = 0; i < kTmemSlots; ++i) {
+      mbar_init(smem_u32(&t_full[i]), 1);
+      mbar_init(smem_u32(&t_empty[i]), 4);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_q);
+    tma_prefetch_desc(&tmap_k);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  WaitCtx wc{p.status, abort_flag, p.budget};
+  const int total_work = g.Hkv * g.Nt;
+
+  if (warp == 0) {
+    // ======================= TMA producer =================================
+    if (lane == 0) {
+      int qcount = 0;
+      int kuse[C::kKStages];
+      int ktag[C::kKStages];
+#pragma unroll
+      for (int i = 0; i < C::kKStages; ++i) { kuse[i] = 0; ktag[i] = -1; }
+      bool ok = true;
+      for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x) {
+        const Item it = make_item(p, w);
+        if (it.n_mt == 0) continue;
+        for (int c = 0; c < p.n_chunks && ok; ++c) {
+          const int qs = qcount % C::kQStages;
+          ok = mbar_wait(smem_u32(&q_empty[qs]), ((qcount / C::kQStages) & 1) ^ 1, wc);
+          if (!ok) break;
+          ++qcount;
+          const uint32_t qb = smem_u32(&q_full[qs]);
+          mbar_arrive_expect_tx(qb, (uint32_t)(p.NC * D * 2));
+          const int P0 = c * p.NC;
+          const int g0 = P0 / g.tile_q, p0 = P0 % g.tile_q;
+#pragma unroll
+          for (int hh = 0; hh < C::kHalves; ++hh)
+            tma_load_3d(q_smem + qs * C::kQBytes + hh * p.NC * 128, &tmap_q, qb, hh * 64,
+                        it.t * g.tile_q + p0, it.h * g.G + g0);
+          for (int m = 0; m < it.n_mt; ++m) {
+            const int s = m % C::kKStages;
+            ok = mbar_wait(smem_u32(&k_empty[s]), (kuse[s] & 1) ^ 1, wc);
+            if (!ok) break;
+            ++kuse[s];
+            const int tag = it.h * 4096 + m;
+            const uint32_t kb = smem_u32(&k_full[s]);
+            if (ktag[s] == tag) {
+              mbar_arrive(kb);   // tile still resident
+            } else {
+              ktag[s] = tag;
+              mbar_arrive_expect_tx(kb, (uint32_t)(128 * D * 2));
+#pragma unroll
+              for (int hh = 0; hh < C::kHalves; ++hh)
+                tma_load_3d(k_smem + s * C::kKBytes + hh * 128 * 128, &tmap_k, kb, hh * 64, m * 128,
+                            it.h);
+            }
+          }
+        }
+      }
+      // Drain: wait (bounded) for every armed barrier phase so no bulk copy is
+      // still writing shared memory when the CTA retires.
+      for (int i = 0; i < C::kKStages; ++i)
+        if (kuse[i] > 0) mbar_wait(smem_u32(&k_full[i]), (kuse[i] - 1) & 1, wc, false);
+      for (int i = 0; i < C::kQStages && i < qcount; ++i) {
+        const int uses = (qcount - i + C::kQStages - 1) / C::kQStages;
+        mbar_wait(smem_u32(&q_full[i]), (uses - 1) & 1, wc, false);
+      }
+    }
+  } else if (warp == 1) {
+    // ======================= MMA issuer ===================================
+    if (lane == 0) {
+      int qcount = 0, tcount = 0;
+      int kuse[C::kKStages];
+#pragma unroll
+      for (int i = 0; i < C::kKStages; ++i) kuse[i] = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x) {
+        const Item it = make_item(p, w);
+        if (it.n_mt == 0) continue;
+        for (int c = 0; c < p.n_chunks && ok; ++c) {
+          const int qs = qcount % C::kQStages;
+          ok = mbar_wait(smem_u32(&q_full[qs]), (qcount / C::kQStages) & 1, wc);
+          if (!ok) break;
+          ++qcount;
+          for (int m = 0; m < it.n_mt; ++m) {
+            const int s = m % C::kKStages;
+            ok = mbar_wait(smem_u32(&k_full[s]), kuse[s] & 1, wc);
+            if (!ok) break;
+            ++kuse[s];
+            const int ts = tcount % kTmemSlots;
+            ok = mbar_wait(smem_u32(&t_empty[ts]), ((tcount / kTmemSlots) & 1) ^ 1, wc);
+            if (!ok) break;
+            ++tcount;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + ts * 128;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const int hh = kk / 4, sub = kk % 4;
+              const uint64_t a_desc =
+                  sw128_desc(k_smem + s * C::kKBytes + hh * 128 * 128 + sub * 32, 16, 1024);
+              const uint64_t b_desc =
+                  sw128_desc(q_smem + qs * C::kQBytes + hh * p.NC * 128 + sub * 32, 16, 1024);
+              umma_ss(d_tmem, a_desc, b_desc, p.idesc, kk > 0 ? 1u : 0u);
+            }
+            umma_commit(smem_u32(&t_full[ts]));
+            umma_commit(smem_u32(&k_empty[s]));
+          }
+          if (ok) umma_commit(smem_u32(&q_empty[qs]));
+        }
+      }
+      // Drain: every MMA issued by this thread has completed once `drain` flips.
+      umma_commit(smem_u32(drain));
+      mbar_wait(smem_u32(drain), 0, wc, false);
+    }
+  } else {
+    // ======================= energy + finalize =============================
+    const int et = threadIdx.x - 64;           // 0..127
+    const int quarter = warp & 3;              // TMEM lane group of this warp
+    const int ew = et >> 5;                    // 0..3 index among energy warps
+    const unsigned lt = (1u << lane) - 1u;
+    int tcount = 0;
+    bool ok = true;   // after a failed wait the role keeps its barrier schedule but skips TMEM
+    for (int w = blockIdx.x; w < total_work; w += gridDim.x) {
+      const Item it = make_item(p, w);
+      const long long row_base = ((long long)it.h * g.Nt + it.t) * Nb;
+      for (int c = 0; c < p.n_chunks; ++c) {
+        for (int m = 0; m < it.n_mt; ++m) {
+          const int ts = tcount % kTmemSlots;
+          if (ok) ok = mbar_wait(smem_u32(&t_full[ts]), (tcount / kTmemSlots) & 1, wc);
+          ok = __all_sync(0xffffffffu, ok);   // the TMEM loads below are warp-collective
+          ++tcount;
+          tc_fence_after();
+          const int b = m * 128 + quarter * 32 + lane;
+          if (ok && m * 128 + quarter * 32 < it.n_full) {
+            float mb = -INFINITY, eb = 0.f;
+            if (c > 0 && b < it.n_full) {
+              const float2 st = stats[b];
+              mb = st.x;
+              eb = st.y;
+            }
+            const long long bstart = (long long)b * g.block_k;
+            const bool bvalid = b < it.n_full;
+            for (int col0 = 0; col0 < p.NC; col0 += 32) {
+              uint32_t r[32];
+              tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + ts * 128 + col0, r);
+              tmem_wait_ld();
+              reg_fence(r);
+              float x[32];
+              float cmax = -INFINITY;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                bool v = bvalid;
+                if (it.row_mask) {
+                  const int P = c * p.NC + col0 + j;
+                  const long long row = (long long)it.t * g.tile_q + P % g.tile_q;
+                  v = v && row < g.valid_lq && bstart <= g.offset + row;
+                }
+                x[j] = v ? __uint_as_float(r[j]) * p.scale_log2 : -INFINITY;
+                cmax = fmaxf(cmax, x[j]);
+              }
+              const float mnew = fmaxf(mb, cmax);
+              if (mnew != -INFINITY) {
+                float acc = 0.f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) acc += ex2(x[j] - mnew);
+                eb = eb * ex2(mb - mnew) + acc;
+                mb = mnew;
+              }
+            }
+            if (bvalid) stats[b] = make_float2(mb, eb);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&t_empty[ts]));
+        }
+      }
+
+      // ---- finalize: tile max, energies, threshold, forcing, lists --------
+      named_bar_sync(1, 128);
+      float lm = -INFINITY;
+      for (int b = et; b < it.n_full; b += 128) lm = fmaxf(lm, stats[b].x);
+      lm = warp_max(lm);
+      if (lane == 0) red[ew] = lm;
+      named_bar_sync(1, 128);
+      const float Mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+      float le = 0.f;
+      for (int b = et; b < it.n_full; b += 128) {
+        const float2 st = stats[b];
+        const float E = (Mx == -INFINITY || st.x == -INFINITY) ? 0.f : st.y * ex2(st.x - Mx);
+        stats[b].y = E;
+        le = fmaxf(le, E);
+      }
+      le = warp_max(le);
+      named_bar_sync(1, 128);
+      if (lane == 0) red[4 + ew] = le;
+      named_bar_sync(1, 128);
+      const float emax = fmaxf(fmaxf(red[4], red[5]), fmaxf(red[6], red[7]));
+      const float thr = g.alpha * emax;
+      const bool dense_tail = it.t >= max(g.Nt - g.last_n, 0);
+      for (int base_b = ew * 32; base_b < Nb; base_b += 128) {
+        const int b = base_b + lane;
+        const long long bs = (long long)b * g.block_k, be = bs + g.block_k;
+        const float E = b < it.n_full ? stats[b].y : 0.f;
+        const bool forced = bs < g.sink || be > it.tile_first - g.window || dense_tail;
+        const bool fin = b < Nb && (E >= thr || forced) && bs <= it.tile_last;
+        const bool pr = b < Nb && !fin && min(be, (long long)g.valid_lk) <= it.tile_first;
+        const unsigned sb = __ballot_sync(0xffffffffu, fin);
+        const unsigned pb = __ballot_sync(0xffffffffu, pr);
+        if (lane == 0) {
+          selw[base_b >> 5] = sb;
+          prw[base_b >> 5] = pb;
+        }
+        if (p.mask != nullptr && b < Nb) p.mask[row_base + b] = (uint8_t)fin;
+      }
+      named_bar_sync(1, 128);
+      if (p.sel_ids != nullptr) {
+        if (ew == 0) {
+          int run_s = 0, run_p = 0;
+          for (int w0 = 0; w0 < nwords; w0 += 32) {
+            const int wi = w0 + lane;
+            const int cs = wi < nwords ? __popc(selw[wi]) : 0;
+            const int cp = wi < nwords ? __popc(prw[wi]) : 0;
+            int is = cs, ip = cp;   // inclusive warp scan
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const int ys = __shfl_up_sync(0xffffffffu, is, o);
+              const int yp = __shfl_up_sync(0xffffffffu, ip, o);
+              if (lane >= o) { is += ys; ip += yp; }
+            }
+            if (wi < nwords) {
+              selpre[wi] = run_s + is - cs;
+              prpre[wi] = run_p + ip - cp;
+            }
+            run_s += __shfl_sync(0xffffffffu, is, 31);
+            run_p += __shfl_sync(0xffffffffu, ip, 31);
+          }
+          if (lane == 0) {
+            totals[0] = run_s;
+            totals[1] = run_p;
+          }
+        }
+        named_bar_sync(1, 128);
+        const int nsel = totals[0], npr = totals[1];
+        for (int base_b = ew * 32; base_b < Nb; base_b += 128) {
+          const int b = base_b + lane;
+          if (b < Nb) {
+            const int wi = base_b >> 5;
+            const uint32_t sb = selw[wi], pb = prw[wi];
+            const int rs = selpre[wi] + __popc(sb & lt);
+            const int rp = prpre[wi] + __popc(pb & lt);
+            p.sel_ids[row_base + (((sb >> lane) & 1u) ? rs : nsel + (b - rs))] = b;
+            p.pr_ids[row_base + (((pb >> lane) & 1u) ? rp : npr + (b - rp))] = b;
+          }
+        }
+        if (et == 0) {
+          p.sel_counts[(long long)it.h * g.Nt + it.t] = nsel;
+          p.pr_counts[(long long)it.h * g.Nt + it.t] = npr;
+        }
+      }
+      named_bar_sync(1, 128);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+}
+
+template <int D>
+size_t smem_bytes(int Nb) {
+  const int nwords = (Nb + 31) / 32;
+  size_t s = 1024 + Cfg<D>::kOpBytes;
+  s += (size_t)Nb * 8 + (size_t)nwords * 16;
+  s += 8 + 8 * (2 * Cfg<D>::kQStages + 2 * Cfg<D>::kKStages + 2 * kTmemSlots + 1);
+  s += 8 + 8 * 4 + 8;
+  return s;
+}
+
+}  // namespace
+
+bool select_tc_supported(const SelectGeom& g, int dt) {
+  if (dt != DT_BF16 && dt != DT_F16) return false;
+  if (g.D != 64 && g.D != 128) return false;
+  if (g.Nb > kMaxNb || g.Nb <= 0) return false;
+  const int R = g.G * g.tile_q;
+  if (R >= 128) {
+    if (R % 128) return false;
+    if (g.tile_q % 128 != 0 && 128 % g.tile_q != 0) return false;
+  } else {
+    if (R % 16) return false;
+  }
+  if (g.tile_q > 256) return g.tile_q % 128 == 0;
+  return true;
+}
+
+cudaError_t launch_select_tc(const SelectTcArgs& a, const void* q, const void* pk,
+                             const TcLaunch& L, cudaStream_t stream) {
+  const SelectGeom& g = a.g;
+  Params p;
+  p.g = g;
+  p.NC = a.NC;
+  p.box_rows = a.box_rows;
+  p.n_chunks = (g.G * g.tile_q) / a.NC;
+  p.idesc = umma_idesc_f16(a.dt == DT_BF16 ? 1 : 0, 128, a.NC, 0, 0);
+  p.scale_log2 = g.scale * kLog2e;
+  p.mask = a.mask;
+  p.sel_ids = a.sel_ids;
+  p.sel_counts = a.sel_counts;
+  p.pr_ids = a.pr_ids;
+  p.pr_counts = a.pr_counts;
+  p.status = L.status;
+  p.budget = L.budget;
+
+  CUtensorMap tq, tk;
+  if (!encode_tmap_3d(&tq, q, a.dt, (uint64_t)g.D, (uint64_t)g.Lq_pad, (uint64_t)g.Hq, 64,
+                      (uint32_t)a.box_rows, (uint32_t)a.box_heads))
+    return cudaErrorInvalidValue;
+  if (!encode_tmap_3d(&tk, pk, a.dt, (uint64_t)g.D, (uint64_t)g.Nb, (uint64_t)g.Hkv, 64, 128, 1))
+    return cudaErrorInvalidValue;
+
+  const int total = g.Hkv * g.Nt;
+  int grid;
+  if (g.Hkv <= L.num_sms) {
+    const int per_head = max(1, min(L.num_sms / g.Hkv, g.Nt));
+    grid = per_head * g.Hkv;
+  } else {
+    grid = L.num_sms;
+  }
+  grid = max(1, min(grid, total));
+  cudaError_t e;
+  if (g.D == 64) {
+    const size_t smem = smem_bytes<64>(g.Nb);
+    e = cudaFuncSetAttribute(select_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    if (e != cudaSuccess) return e;
+    select_tc_kernel<64><<<grid, kThreads, smem, stream>>>(tq, tk, p);
+  } else {
+    const size_t smem = smem_bytes<128>(g.Nb);
+    e = cudaFuncSetAttribute(select_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    if (e != cudaSuccess) return e;
+    select_tc_kernel<128><<<grid, kThreads, smem, stream>>>(tq, tk, p);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace fpv2

@@ -1,0 +1,171 @@
+/*
+ * fpv2_b200.h - C ABI of the B200 (sm_100a) FlashPrefill V2 prefill-attention path.
+ *
+ * Every entry point is stream-ordered and asynchronous: it validates its
+ * scalar arguments, enqueues its kernels on `stream` (a cudaStream_t passed
+ * as void*, NULL = legacy default stream) and returns. Nothing here
+ * synchronises the host, and no entry point allocates device memory: the
+ * caller owns every input, output and the stream.
+ *
+ * Tensors are dense, row-major, device-resident:
+ *   q            [q_heads,  padded_q_len, head_dim]
+ *   k, v         [kv_heads, padded_k_len, head_dim]
+ *   pooled_k/v   [kv_heads, num_blocks,   head_dim]   num_blocks = padded_k_len / block_k
+ *   selected     uint8 (0/1) [kv_heads, num_tiles, num_blocks], num_tiles = padded_q_len / tile_q
+ *   *_ids        int32 [kv_heads, num_tiles, num_blocks]   (full-width padded lists)
+ *   *_counts     int32 [kv_heads, num_tiles]
+ * Query row r of q head hq belongs to KV head hq / (q_heads / kv_heads); a
+ * selection tile packs the tile_q rows of all q heads of one KV head.
+ *
+ * Return value: FPV2_OK or an FPV2_ERR_* code; fpv2_last_error() gives the
+ * message of the calling thread's last failure.
+ */
+#ifndef FPV2_B200_H
+#define FPV2_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FPV2_API __attribute__((visibility("default")))
+#else
+#define FPV2_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define FPV2_F16 0
+#define FPV2_BF16 1
+#define FPV2_F32 2
+
+/* status codes */
+#define FPV2_OK 0
+#define FPV2_ERR_INVALID_ARGUMENT 1 /* a shape, pointer or scalar is out of contract */
+#define FPV2_ERR_UNSUPPORTED 2      /* valid request this build cannot run (device, dtype) */
+#define FPV2_ERR_CUDA 3             /* a CUDA runtime call or kernel launch failed */
+#define FPV2_ERR_DEVICE_TIMEOUT 4   /* a kernel's bounded wait expired (see fpv2_device_status) */
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+FPV2_API int fpv2_version(void);
+
+/* Message of the calling thread's most recent failed call ("" if none). */
+FPV2_API const char* fpv2_last_error(void);
+
+/* FPV2_OK when `device` is an sm_100 GPU this build can run on. */
+FPV2_API int fpv2_device_supported(int device);
+
+/*
+ * Device status word of the current device. Kernels that give up a bounded
+ * wait set a bit here instead of hanging; this call synchronises `stream`,
+ * returns the word and clears it when `clear` is non-zero.
+ */
+FPV2_API int fpv2_device_status(void* stream, int clear, int32_t* status_out);
+
+/* Upper bound, in milliseconds, for any single wait inside a kernel (default 2000). */
+FPV2_API int fpv2_set_wait_budget_ms(double milliseconds);
+
+/*
+ * Mean-pool the sequence axis of x [heads, length, head_dim] into blocks of
+ * block_size rows: out [heads, length / block_size, head_dim].
+ * The mean is exact (float64 sum), rounded to float32, then to out_dtype.
+ * Replaces fpv2/selection.py:68-80 (pool_blocks).
+ */
+FPV2_API int fpv2_pool_blocks(const void* x, int x_dtype, int64_t heads, int64_t length,
+                     int32_t head_dim, int32_t block_size, void* out, int out_dtype,
+                     void* stream);
+
+/*
+ * Index stage on caller-pooled keys: selection mask [kv_heads, num_tiles, num_blocks].
+ * Scores are scale * q . pooled_k in float32; per (KV head, tile) the block
+ * energies sum exp(score - tile max) over the tile's fully visible blocks and
+ * visible rows; a block is kept when its energy is >= alpha * max energy, and
+ * sink / local-window / diagonal / dense-tail blocks are forced, all limited
+ * to causally visible blocks. `offset` is the absolute key position of query
+ * row 0; rows >= query_length are padding. `raw_scores` (nullable) receives
+ * the unmasked scale * q . pooled_k scores [kv_heads, G, padded_q_len, num_blocks].
+ * Replaces fpv2/selection.py:109-201 (block_scores_and_select).
+ */
+FPV2_API int fpv2_block_select(const void* q, int q_dtype, const void* pooled_k, int k_dtype,
+                      int32_t q_heads, int32_t kv_heads, int32_t padded_q_len,
+                      int32_t num_blocks, int32_t head_dim, int32_t offset,
+                      int32_t query_length, float scale, int32_t block_k, int32_t tile_q,
+                      float alpha, int32_t sink_tokens, int32_t window_tokens,
+                      int32_t last_n_blocks, uint8_t* selected, float* raw_scores,
+                      void* stream);
+
+/*
+ * Mask -> padded block lists. selected_ids lists the selected blocks
+ * ascending followed by every other block ascending; pruned_ids likewise for
+ * the blocks that are not selected and end (clamped to key_length) at or
+ * before the tile's first query position.
+ * Replaces fpv2/kernel.py:141-184 (compact_block_indices).
+ */
+FPV2_API int fpv2_compact_block_indices(const uint8_t* selected, int32_t kv_heads, int32_t num_tiles,
+                               int32_t num_blocks, int32_t block_k, int32_t tile_q,
+                               int32_t offset, int32_t query_length, int32_t key_length,
+                               int32_t* selected_ids, int32_t* selected_counts,
+                               int32_t* pruned_ids, int32_t* pruned_counts, void* stream);
+
+/*
+ * Fused index stage of the attention hook: pools K and V into pooled_k /
+ * pooled_v (written as `pooled_dtype`: the input dtype, as fpv2/patch.py:137-138
+ * pools, or FPV2_F32, as fpv2/reference.py:45-48 pools), selects on those
+ * pooled keys and writes the four list/count arrays. `selected` (nullable)
+ * also receives the mask.
+ * Replaces the pool_blocks x2 -> block_scores_and_select -> compact_block_indices
+ * sequence of fpv2/patch.py:137-153.
+ */
+FPV2_API int fpv2_index_stage(const void* q, const void* k, const void* v, int dtype,
+                     int32_t q_heads, int32_t kv_heads, int32_t padded_q_len,
+                     int32_t padded_k_len, int32_t head_dim, int32_t offset,
+                     int32_t query_length, int32_t key_length, float scale,
+                     int32_t block_k, int32_t tile_q, float alpha, int32_t sink_tokens,
+                     int32_t window_tokens, int32_t last_n_blocks, int pooled_dtype,
+                     void* pooled_k, void* pooled_v, int32_t* selected_ids,
+                     int32_t* selected_counts, int32_t* pruned_ids, int32_t* pruned_counts,
+                     uint8_t* selected, void* stream);
+
+/*
+ * Block-sparse attention over the lists: per query row, online softmax in
+ * base 2 over the selected blocks (causal and key_length masked), then, when
+ * mean_correction is set, the pruned blocks as pooled K/V entries with logits
+ * shifted by log2(block_k). q/k/v/out share `dtype` (FPV2_F16 or FPV2_BF16);
+ * pooled_k/pooled_v are `pooled_dtype` (dtype or FPV2_F32) and are rounded
+ * to `dtype` on load. Ids are clipped to [0, num_blocks-1] and counts to
+ * [0, num_blocks]. Rows >= query_length are padding; their output is unspecified.
+ * Replaces fpv2/kernel.py:441-590 (sparse_attention) and its Metal kernel
+ * fpv2/kernel.py:187-414.
+ */
+FPV2_API int fpv2_sparse_attention(const void* q, const void* k, const void* v, const void* pooled_k,
+                          const void* pooled_v, int pooled_dtype,
+                          const int32_t* selected_ids, const int32_t* selected_counts,
+                          const int32_t* pruned_ids, const int32_t* pruned_counts, int dtype,
+                          int32_t q_heads, int32_t kv_heads, int32_t padded_q_len,
+                          int32_t padded_k_len, int32_t head_dim, int32_t offset,
+                          int32_t query_length, int32_t key_length, float scale,
+                          int32_t block_k, int32_t tile_q, int32_t mean_correction,
+                          void* out, void* stream);
+
+/*
+ * Which kernel family the two stages would use for this shape:
+ * bit 0 set = tcgen05 index stage, bit 1 set = tcgen05 attention
+ * (otherwise the generic CUDA-core kernels run).
+ */
+FPV2_API int fpv2_fast_path_mask(int dtype, int32_t q_heads, int32_t kv_heads, int32_t head_dim,
+                        int32_t block_k, int32_t tile_q, int32_t num_blocks);
+
+/*
+ * Test hook for failure detection: launches one CTA that waits on an
+ * mbarrier nothing ever arrives at, with a budget of `budget_ms`. Returns
+ * FPV2_ERR_DEVICE_TIMEOUT (and leaves the context usable) when the bounded
+ * wait gave up as designed.
+ */
+FPV2_API int fpv2_selftest_wait_timeout(double budget_ms, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FPV2_B200_H */

@@ -1,0 +1,85 @@
+"""Comparison helpers shared by the GPU parity tests, ``smoke()`` and the benchmark.
+
+All checks compare the CUDA path with the CPU oracle (oracle/fpv2_oracle.py) on
+identical inputs:
+
+* pooled K/V: bit-exact;
+* selection masks: bit-exact except blocks whose float64 energy lies within a
+  relative 1e-5 of the alpha threshold (reported as flips);
+* lists: bit-exact compaction of the mask (full padded width) and, when no
+  block flipped, bit-exact against the oracle's lists;
+* attention output: max-abs <= 2e-2 and mean-abs <= 2e-3 against the float32
+  reference math of fpv2/reference.py.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, replace
+
+import numpy as np
+import torch
+
+from oracle import fpv2_oracle as O
+
+MAX_ABS_TOL = 2e-2
+MEAN_ABS_TOL = 2e-3
+FLIP_REL_BAND = 1e-5
+
+_DT = {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}
+
+
+def np32(t: torch.Tensor) -> np.ndarray:
+    return t.detach().to("cpu", torch.float32).numpy()
+
+
+def dtname(dtype: torch.dtype) -> str:
+    return _DT[dtype]
+
+
+@dataclass
+class SelectCheck:
+    mismatches: int
+    flips_in_band: int
+    out_of_band: int
+    band_blocks: int
+
+    @property
+    def ok(self) -> bool:
+        return self.out_of_band == 0
+
+
+def check_selection(q: torch.Tensor, pooled_k_np: np.ndarray, gpu_mask: np.ndarray, *, scale: float,
+                    config, offset: int = 0, query_length: int | None = None) -> SelectCheck:
+    """GPU mask vs the oracle on the same pooled keys, flips allowed only in the fp64 band."""
+    c = O.as_config(config)
+    chunk = replace(c, score_chunk_tiles=c.score_chunk_tiles or max(1, 4096 // c.tile_q))
+    qf = np32(q)
+    r32 = O.block_scores_and_select(qf, pooled_k_np, scale=scale, config=chunk, offset=offset,
+                                    query_length=query_length)
+    r64 = O.block_scores_and_select(qf, pooled_k_np, scale=scale, config=chunk, offset=offset,
+                                    query_length=query_length, precision="fp64")
+    band = O.threshold_band(r64, FLIP_REL_BAND)
+    diff = gpu_mask != r32.selected
+    return SelectCheck(
+        mismatches=int(diff.sum()),
+        flips_in_band=int((diff & band).sum()),
+        out_of_band=int((diff & ~band).sum()),
+        band_blocks=int(band.sum()),
+    )
+
+
+def check_lists_of_mask(mask: np.ndarray, lists, *, config, offset: int, query_length: int,
+                        key_length: int) -> bool:
+    """GPU lists equal the oracle's compaction of the same mask, full padded width."""
+    ref = O.compact_block_indices(mask.astype(bool), config=config, offset=offset,
+                                  query_length=query_length, key_length=key_length)
+    return all(np.array_equal(a.cpu().numpy(), b) for a, b in zip(lists, ref))
+
+
+def attention_errors(actual: torch.Tensor, expected: np.ndarray, rows: int | None = None):
+    a = np32(actual)
+    if rows is not None:
+        a = a[:, :rows]
+        expected = expected[:, :rows]
+    err = np.abs(a - expected)
+    return float(err.max()), float(err.mean())

@@ -1,0 +1,157 @@
+"""Host logic and the C-ABI boundary, without a GPU.
+
+Checks the reference's validation messages, the hook's config resolution, that
+the library loads and exports every symbol declared in include/fpv2_b200.h, and
+that CPU tensors are rejected instead of silently computed elsewhere.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+import fpv2
+from fpv2 import _lib
+from fpv2.kernel import TileConfig, _tile_for_config
+from fpv2.patch import _causal_block_count, _causal_offset, _effective_config, _request_config
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_symbols() -> list[str]:
+    header = (ROOT / "include" / "fpv2_b200.h").read_text()
+    return re.findall(r"FPV2_API\s+(?:const\s+char\s*\*|int)\s+(fpv2_\w+)\s*\(", header)
+
+
+def test_library_exports_every_declared_symbol():
+    names = declared_symbols()
+    assert len(names) >= 10
+    handle = ctypes.CDLL(str(_lib.LIB_PATH))
+    for name in names:
+        assert hasattr(handle, name), name
+    assert set(names) == set(_lib.EXPORTED_SYMBOLS)
+    assert _lib.lib().fpv2_version() >= 100
+
+
+def test_fast_path_selection_rules_without_gpu():
+    assert _lib.fast_path_mask(torch.bfloat16, 32, 8, 128, 128, 32, 512) == 3
+    assert _lib.fast_path_mask(torch.float16, 64, 8, 128, 128, 16, 1024) == 3
+    assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 128, 128, 128, 16) == 3   # direct tile_q 128
+    assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 96, 128, 32, 16) == 0
+    assert _lib.fast_path_mask(torch.bfloat16, 4, 2, 64, 16, 16, 4) == 1       # select tc, attn generic
+    assert _lib.fast_path_mask(torch.float32, 8, 2, 128, 128, 32, 16) == 0
+
+
+def test_invalid_arguments_return_status_without_gpu():
+    rc = _lib.lib().fpv2_pool_blocks(None, 1, 2, 7, 4, 4, None, 1, None)
+    assert rc == _lib.ERR_INVALID_ARGUMENT
+    assert "divisible" in _lib.lib().fpv2_last_error().decode()
+
+
+def test_cpu_tensors_are_rejected():
+    with pytest.raises(ValueError, match="CUDA"):
+        fpv2.pool_blocks(torch.zeros(2, 8, 4), 4)
+    q = torch.zeros(4, 16, 8)
+    with pytest.raises(ValueError, match="CUDA"):
+        fpv2.block_scores_and_select(q, torch.zeros(2, 1, 8), scale=1.0,
+                                     config=fpv2.FPV2Config(block_k=16, tile_q=16))
+
+
+def test_pool_blocks_rejects_unaligned_length():
+    with pytest.raises(ValueError, match="divisible"):
+        fpv2.pool_blocks(torch.zeros((2, 7, 4)), 4)
+
+
+@pytest.mark.parametrize("value", [0, -1, 1.5, True])
+def test_score_chunk_tiles_must_be_a_positive_integer(value):
+    with pytest.raises(ValueError, match="score_chunk_tiles"):
+        fpv2.FPV2Config(score_chunk_tiles=value)
+
+
+def test_pack_gqa_must_be_boolean():
+    with pytest.raises(ValueError, match="pack_gqa"):
+        fpv2.FPV2Config(pack_gqa=1)
+
+
+@pytest.mark.parametrize("value", [-1, 1.5, True])
+def test_last_n_blocks_must_be_a_non_negative_integer(value):
+    with pytest.raises(ValueError, match="last_n_blocks"):
+        fpv2.FPV2Config(last_n_blocks=value)
+
+
+def test_hopper_selection_defaults():
+    c = fpv2.FPV2Config()
+    assert c.window_tokens == 384 and c.last_n_blocks == 2
+
+
+def test_compaction_rejects_non_boolean_mask():
+    with pytest.raises(ValueError, match="boolean"):
+        fpv2.compact_block_indices(torch.ones((1, 1, 1), dtype=torch.int32))
+
+
+def test_default_tile_dispatch():
+    assert fpv2.default_tile(64) == TileConfig(32, 32, 4)
+    assert fpv2.default_tile(96) == TileConfig(32, 32, 4)
+    assert fpv2.default_tile(128) == TileConfig(64, 32, 8)
+    assert fpv2.default_tile(256) == TileConfig(32, 16, 4)
+    assert _tile_for_config(128, _effective_config(fpv2.FPV2Config(), 32, 8)) == TileConfig(32, 16, 4)
+
+
+def test_default_tile_uses_128_packed_gqa_rows():
+    effective = _effective_config(fpv2.FPV2Config(), query_heads=32, kv_heads=8)
+    assert effective is not None and effective.tile_q == 32
+    custom = fpv2.FPV2Config(tile_q=64)
+    assert _effective_config(custom, query_heads=32, kv_heads=8) is custom
+    assert _effective_config(fpv2.FPV2Config(), query_heads=16, kv_heads=8).tile_q == 64
+    assert _effective_config(fpv2.FPV2Config(), query_heads=24, kv_heads=8) is None   # G = 3
+
+
+def test_dense_tail_is_applied_only_at_known_request_end():
+    config = fpv2.FPV2Config(last_n_blocks=2)
+    assert _request_config(config, 2_048, 8_192).last_n_blocks == 0
+    assert _request_config(config, 8_192, 8_192) is config
+    assert _request_config(config, 8_192, None).last_n_blocks == 0
+
+
+def test_causal_block_count():
+    c = _effective_config(fpv2.FPV2Config(), 4, 2)   # tile_q 64
+    assert _causal_block_count(2, 256, 0, c) == 12
+    assert _causal_block_count(2, 128, 0, c) == 4
+
+
+def test_causal_alignment_rules():
+    from torch.nn.attention.bias import causal_lower_right, causal_upper_left
+
+    q = torch.zeros(1, 4, 128, 64)
+    k = torch.zeros(1, 2, 256, 64)
+    assert _causal_offset(q, q, None, True) == 0
+    assert _causal_offset(q, k, None, True) is None          # top-left alignment: not ours
+    assert _causal_offset(q, k, causal_lower_right(128, 256), False) == 128
+    assert _causal_offset(q, k, causal_upper_left(128, 256), False) is None
+    assert _causal_offset(q, k, torch.zeros(128, 256), False) is None
+
+
+@pytest.mark.parametrize("value", [0, -1, 1.5, True])
+def test_total_tokens_must_be_a_positive_integer(value):
+    with pytest.raises(ValueError, match="total_tokens"):
+        fpv2.enable(total_tokens=value)
+    fpv2.disable()
+
+
+def test_enable_disable_restores_original():
+    import torch.nn.functional as F
+
+    from fpv2.patch import _ORIGINAL_SDPA
+
+    fpv2.enable(min_tokens=1)
+    assert fpv2.is_enabled() and F.scaled_dot_product_attention is not _ORIGINAL_SDPA
+    q = torch.randn(1, 2, 8, 16)
+    # CPU tensors fall through to the original function, bit for bit
+    out = F.scaled_dot_product_attention(q, q, q, is_causal=True)
+    assert torch.equal(out, _ORIGINAL_SDPA(q, q, q, is_causal=True))
+    fpv2.disable()
+    assert not fpv2.is_enabled() and F.scaled_dot_product_attention is _ORIGINAL_SDPA

@@ -1,0 +1,226 @@
+"""Pin the CPU oracle against the reference's known-answer tests and invariants.
+
+Runs without a GPU. The oracle is the checker for every CUDA parity test, so
+it is pinned here first: every KAT in tests/golden/reference_kats.json
+(transcribed from the reference's tests) and the reference's invariant tests
+(tests/test_reference.py, tests/test_selection.py of the reference).
+"""
+
+from __future__ import annotations
+
+import json
+from dataclasses import replace
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fpv2_oracle as O
+from tests.synthetic import structured_qkv, topic_qkv
+
+KATS = json.loads((Path(__file__).parent / "golden" / "reference_kats.json").read_text())
+
+
+def np32(t: torch.Tensor) -> np.ndarray:
+    return t.to(torch.float32).numpy()
+
+
+def cfg(**kw) -> O.OracleConfig:
+    return O.OracleConfig(**kw)
+
+
+def test_pool_blocks_kat():
+    k = KATS["pool_blocks"]
+    x = np.arange(32, dtype=np.float32).reshape(2, 8, 2)
+    assert np.array_equal(O.pool_blocks(x, k["block_size"]), np.array(k["expected"], np.float32))
+
+
+def test_pool_blocks_rejects_unaligned_length():
+    with pytest.raises(ValueError, match="divisible"):
+        O.pool_blocks(np.zeros((2, 7, 4), np.float32), 4)
+
+
+def test_alpha_zero_selects_exactly_visible_blocks():
+    k = KATS["alpha_zero_lower_triangle"]
+    c = cfg(**k["config"])
+    q, kk, _ = structured_qkv(length=k["length"], query_heads=k["query_heads"],
+                              kv_heads=k["kv_heads"], block_size=c.block_k)
+    res = O.block_scores_and_select(np32(q), O.pool_blocks(np32(kk), c.block_k),
+                                    scale=q.shape[-1] ** -0.5, config=c)
+    expected = np.broadcast_to(np.tril(np.ones((8, 8), bool)), res.selected.shape)
+    assert np.array_equal(res.selected, expected)
+    assert O.density(res.selected, config=c) == pytest.approx(k["density"])
+
+
+def test_partially_visible_block_does_not_set_tile_energy_scale():
+    k = KATS["partially_visible_block"]
+    res = O.block_scores_and_select(np.array(k["q"], np.float32), np.array(k["pooled_k"], np.float32),
+                                    scale=k["scale"], config=cfg(**k["config"]), offset=k["offset"])
+    assert res.selected.tolist() == k["expected"]
+
+
+def test_last_n_blocks_are_fully_dense_for_complete_request():
+    k = KATS["last_n_dense_tail"]
+    q = np.full(k["q_shape"], k["q_fill"], np.float32)
+    pk = np.full(k["pooled_k_shape"], k["pooled_k_fill"], np.float32)
+    res = O.block_scores_and_select(q, pk, scale=k["scale"], config=cfg(**k["config"]))
+    assert res.selected.tolist() == k["expected"]
+
+
+def test_defaults():
+    c = O.OracleConfig()
+    assert c.window_tokens == KATS["defaults"]["window_tokens"]
+    assert c.last_n_blocks == KATS["defaults"]["last_n_blocks"]
+
+
+def test_compaction_kat():
+    k = KATS["compaction_order"]
+    ids, counts, _, _ = O.compact_block_indices(np.array(k["selected"]), config=cfg(**k["config"]))
+    assert counts.item() == k["count"]
+    assert ids[0, 0, : k["count"]].tolist() == k["prefix"]
+
+
+def test_compaction_rejects_non_boolean_mask():
+    with pytest.raises(ValueError, match="boolean"):
+        O.compact_block_indices(np.ones((1, 1, 1), np.int32))
+
+
+def test_compaction_stable_padding_order():
+    sel = np.array([[[False, True, False, True, True]]])
+    ids, counts, pids, pcounts = O.compact_block_indices(
+        sel, config=cfg(block_k=4, tile_q=4), offset=16)
+    assert ids.tolist() == [[[1, 3, 4, 0, 2]]] and counts.item() == 3
+    # pruned: not selected and fully past tile_first = 16 -> blocks 0 and 2
+    assert pids.tolist() == [[[0, 2, 1, 3, 4]]] and pcounts.item() == 2
+
+
+def test_effective_and_request_config():
+    k = KATS["effective_config"]
+    eff = O.effective_config(O.OracleConfig(), k["query_heads"], k["kv_heads"])
+    assert eff.tile_q == k["tile_q"]
+    custom = O.OracleConfig(tile_q=k["custom_tile_q"])
+    assert O.effective_config(custom, k["query_heads"], k["kv_heads"]) == custom
+    for key_length, total, expected in KATS["request_config"]["cases"]:
+        assert O.request_config(O.OracleConfig(last_n_blocks=2), key_length, total).last_n_blocks == expected
+
+
+def test_block_sparsity_counts_kat():
+    """Hook stats of tests/test_patch.py:180-201 restated on the oracle."""
+    k = KATS["block_sparsity"]
+    base = O.OracleConfig(**k["config"])
+    eff = O.effective_config(base, k["query_heads"], k["kv_heads"])
+    q, kk, v = [t.numpy() for t in (torch.randn(1, 4, 256, 64), torch.randn(1, 2, 256, 64),
+                                    torch.randn(1, 2, 256, 64))]
+    _, sel, lists = O.fpv2_sdpa(q, kk, v, scale=64 ** -0.5, config=base, dtype="fp32")
+    visible = O.causal_block_count(k["kv_heads"], k["first_length"], 0, eff)
+    selected = int(lists[1].sum())
+    assert 1 - selected / visible == pytest.approx(k["expected_first"])
+    dense = O.causal_block_count(k["kv_heads"], k["second_length"], 0, eff)
+    assert 1 - (selected + dense) / (visible + dense) == pytest.approx(k["expected_second"])
+
+
+def test_chunked_scoring_matches_unchunked_selection():
+    c = cfg(block_k=16, tile_q=16, alpha=0.35, sink_tokens=16, window_tokens=32)
+    q, k, _ = structured_qkv(length=160, query_heads=8, kv_heads=2, block_size=16, seed=7)
+    pk = O.pool_blocks(np32(k), 16)
+    a = O.block_scores_and_select(np32(q), pk, scale=q.shape[-1] ** -0.5, config=c)
+    b = O.block_scores_and_select(np32(q), pk, scale=q.shape[-1] ** -0.5,
+                                  config=replace(c, score_chunk_tiles=3))
+    assert a.raw_scores is not None and b.raw_scores is None
+    assert np.array_equal(a.selected, b.selected)
+
+
+def test_chunked_scoring_preserves_offset_and_padded_query_semantics():
+    c = cfg(block_k=16, tile_q=16, alpha=0.4, sink_tokens=16, window_tokens=16)
+    q, k, _ = structured_qkv(length=160, query_heads=4, kv_heads=2, block_size=16, seed=11)
+    offset, ql = 37, 55
+    pq = np.zeros((4, 64, q.shape[-1]), np.float32)
+    pq[:, :ql] = np32(q)[:, offset:offset + ql]
+    pk = O.pool_blocks(np32(k), 16)
+    a = O.block_scores_and_select(pq, pk, scale=q.shape[-1] ** -0.5, config=c, offset=offset,
+                                  query_length=ql)
+    b = O.block_scores_and_select(pq, pk, scale=q.shape[-1] ** -0.5,
+                                  config=replace(c, score_chunk_tiles=2), offset=offset,
+                                  query_length=ql)
+    assert b.raw_scores is None
+    assert np.array_equal(a.selected, b.selected)
+
+
+def test_dense_selection_matches_exact_causal_attention():
+    """tests/test_reference.py:29-51."""
+    c = cfg(block_k=32, tile_q=32, alpha=0, sink_tokens=0, window_tokens=0, mean_correction=False)
+    q, k, v = structured_qkv(length=256, block_size=32)
+    scale = q.shape[-1] ** -0.5
+    actual = O.fpv2_attention_reference(np32(q), np32(k), np32(v), scale=scale, config=c)
+    expected = O.exact_causal_attention(np32(q), np32(k), np32(v), scale)
+    rel = np.abs(actual - expected).max() / max(np.abs(expected).max(), 1e-8)
+    assert rel < 1e-5
+    res = O.block_scores_and_select(np32(q), O.pool_blocks(np32(k), 32), scale=scale, config=c)
+    assert O.density(res.selected, config=c) == 1.0
+
+
+def test_dense_selection_matches_exact_attention_with_offset():
+    """tests/test_reference.py:71-89."""
+    c = cfg(block_k=128, tile_q=128, alpha=0, sink_tokens=0, window_tokens=0, mean_correction=False)
+    q, k, v = structured_qkv(length=2048, block_size=128, seed=13)
+    off = 1024
+    scale = q.shape[-1] ** -0.5
+    actual = O.fpv2_attention_reference(np32(q)[:, off:], np32(k), np32(v), scale=scale, config=c,
+                                        offset=off)
+    expected = O.exact_causal_attention(np32(q)[:, off:], np32(k), np32(v), scale, off)
+    assert np.allclose(actual, expected, rtol=1e-5, atol=1e-6)
+
+
+def test_mean_correction_improves_sparse_approximation():
+    """tests/test_reference.py:54-68."""
+    base = dict(block_k=32, tile_q=32, alpha=0.6, sink_tokens=32, window_tokens=32)
+    q, k, v = structured_qkv(length=512, block_size=32, noise=0.01)
+    scale = 3.0
+    expected = O.exact_causal_attention(np32(q), np32(k), np32(v), scale)
+    trunc = O.fpv2_attention_reference(np32(q), np32(k), np32(v), scale=scale,
+                                       config=cfg(**base, mean_correction=False))
+    corr = O.fpv2_attention_reference(np32(q), np32(k), np32(v), scale=scale,
+                                      config=cfg(**base, mean_correction=True))
+    assert np.abs(corr - expected).max() <= np.abs(trunc - expected).max()
+
+
+@pytest.mark.parametrize("corr", [False, True])
+def test_blockwise_equals_dense_reference(corr):
+    c = cfg(alpha=0.15, sink_tokens=128, window_tokens=256, mean_correction=corr)
+    q, k, v = topic_qkv(length=1024, query_heads=8, kv_heads=2, seed=3, dtype=torch.float32)
+    scale = 128 ** -0.5
+    dense = O.fpv2_attention_reference(np32(q), np32(k), np32(v), scale=scale, config=c)
+    block = O.fpv2_attention_blockwise(np32(q), np32(k), np32(v), scale=scale, config=c)
+    assert np.abs(dense - block).max() < 1e-5
+
+
+@pytest.mark.parametrize("corr", [False, True])
+def test_list_semantics_match_reference_math(corr):
+    """The list-driven kernel restatement agrees with reference.py within the output tolerance."""
+    c = cfg(alpha=0.15, sink_tokens=128, window_tokens=256, mean_correction=corr)
+    q, k, v = topic_qkv(length=1024, query_heads=8, kv_heads=2, seed=5, dtype=torch.bfloat16)
+    qf, kf, vf = np32(q), np32(k), np32(v)
+    scale = 128 ** -0.5
+    ref = O.fpv2_attention_reference(qf, kf, vf, scale=scale, config=c)
+    pk = O.pool_blocks(kf, 128, "fp32")
+    pv = O.pool_blocks(vf, 128, "fp32")
+    sel = O.block_scores_and_select(qf, pk, scale=scale, config=c).selected
+    lists = O.compact_block_indices(sel, config=c)
+    out = O.sparse_attention(qf, kf, vf, pk, pv, *lists, scale=scale, config=c, dtype="bf16")
+    err = np.abs(out - ref)
+    assert err.max() < 2e-2 and err.mean() < 2e-3
+
+
+def test_round_to_bf16_matches_torch():
+    x = torch.randn(10000) * 100
+    mine = O.round_to_bf16(x.numpy())
+    assert np.array_equal(mine, x.to(torch.bfloat16).to(torch.float32).numpy())
+
+
+def test_pool_rounding_matches_torch_bf16():
+    """pool_blocks(out_dtype=bf16) = exact mean -> fp32 -> bf16, same as torch's rounding."""
+    x = torch.randn(2, 256, 64).to(torch.bfloat16)
+    mine = O.pool_blocks(np32(x), 128, "bf16")
+    ref = x.double().reshape(2, 2, 128, 64).mean(dim=2).float().to(torch.bfloat16).float().numpy()
+    assert np.array_equal(mine, ref)
