@@ -8,7 +8,7 @@
 // A work item is one 128-row chunk of a selection tile: the G query heads of
 // one KV head packed together (GQA packing), so every K/V tile loaded feeds
 // all G heads. Per KV item (one 128-key sub-tile of a selected block, or one
-// chunk of up to 128 pooled entries):
+// 128-row tile of pooled K/V):
 //   S[128x128] = Q . K^T          tcgen05.mma SS, fp32 in TMEM (double buffered)
 //   P = 2^(S*c - m)               softmax warps: TMEM -> regs -> bf16/f16 P back
 //                                 into the same TMEM columns
@@ -16,10 +16,17 @@
 // The running max is rescaled lazily: O in TMEM is only rescaled when a row's
 // max grows by more than 2^8, which leaves the final O/l unchanged.
 //
+// Pooled correction: instead of gathering the pruned blocks' pooled rows, the
+// producer streams contiguous 128-row tiles of the head's pooled K/V with TMA
+// and ships a 128-bit mask per tile (bit = "this pooled entry is in the pruned
+// list"); masked entries take finite_min logits, exactly like list padding in
+// the reference kernel. Tiles without a pruned entry are skipped. (Pooled
+// inputs in float32 are rounded on a gathered path instead.)
+//
 // Warp roles (192 threads, one persistent CTA per SM):
-//   warp 0     producer: walks the lists, publishes one record per KV item,
-//              TMA-loads Q / K / V tiles (128B swizzle) and gathers pooled
-//              K/V rows for correction items with plain loads (no multicast);
+//   warp 0     producer: takes work items from a global counter (largest
+//              first), walks the lists, publishes one record per KV item and
+//              loads Q / K / V / pooled tiles with TMA (no multicast);
 //   warp 1     MMA issuer;
 //   warps 2-5  softmax (thread = query row) and the output epilogue.
 #include "common.cuh"
@@ -34,14 +41,17 @@ constexpr int kStages = 2;      // K/V tiles and S buffers
 constexpr int kRecs = 8;        // item records in flight
 constexpr int kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
+constexpr int kMaskWordsMax = 64;           // pooled-entry mask of one work item (Nb <= 2048)
 
-enum : int { KIND_SEL = 0, KIND_CORR = 1, KIND_EMPTY = 2 };
+enum : int { KIND_SEL = 0, KIND_POOL = 1, KIND_CORR = 2, KIND_EMPTY = 3, KIND_DONE = 4 };
 
 struct Rec {
   int kind;
-  int kstart;   // SEL: first key; CORR: first list entry
-  int nvalid;   // CORR: valid entries in this chunk
-  int last;     // last item of the work item
+  int kstart;     // SEL: first key; POOL: first pooled row; CORR: first list entry
+  int nvalid;     // CORR: valid list entries in this chunk
+  int flags;      // bit 0: first item of the work item, bit 1: last item
+  int w;          // work item index
+  uint32_t mask[4];   // POOL: entry e is a pruned block when bit (e & 31) of mask[e >> 5]
 };
 
 template <int D>
@@ -57,6 +67,7 @@ struct Params {
   int nch;          // 128-row chunks per tile
   int items;        // total work items
   uint32_t idesc_qk, idesc_pv;
+  int* sched;       // work counter (zeroed before launch); null = static round robin
   int* status;
   long long budget;
 };
@@ -71,7 +82,7 @@ __device__ __forceinline__ Chunk make_chunk(const Params& p, int w) {
   const AttnArgs& a = p.a;
   Chunk ck;
   const int per_t = a.Hkv * p.nch;
-  ck.t = a.Nt - 1 - w / per_t;
+  ck.t = a.Nt - 1 - w / per_t;   // latest tiles (most causal work) first
   const int r = w % per_t;
   ck.h = r / p.nch;
   ck.c = r % p.nch;
@@ -79,7 +90,8 @@ __device__ __forceinline__ Chunk make_chunk(const Params& p, int w) {
   ck.g0 = P0 / a.tile_q;
   ck.p0 = P0 % a.tile_q;
   const long long span = min(a.tile_q, 128);
-  const long long last_row = min((long long)ck.t * a.tile_q + ck.p0 + span, (long long)a.valid_lq) - 1;
+  const long long last_row =
+      min((long long)ck.t * a.tile_q + ck.p0 + span, (long long)a.valid_lq) - 1;
   ck.abs_last = (long long)a.offset + last_row;
   return ck;
 }
@@ -90,7 +102,9 @@ template <int D, int DT>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                    const __grid_constant__ CUtensorMap tmap_k,
-                   const __grid_constant__ CUtensorMap tmap_v, Params p) {
+                   const __grid_constant__ CUtensorMap tmap_v,
+                   const __grid_constant__ CUtensorMap tmap_pk,
+                   const __grid_constant__ CUtensorMap tmap_pv, Params p) {
   using C = Cfg<D>;
   const AttnArgs& a = p.a;
   extern __shared__ uint8_t smem_raw[];
@@ -103,7 +117,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t v_smem = k_smem + kStages * C::kTileBytes;       // [kStages][tile]
   uint8_t* after_tiles = gbase + (2 + 2 * kStages) * C::kTileBytes;
   Rec* recs = reinterpret_cast<Rec*>(after_tiles);                // [kRecs]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(recs + kRecs);
+  uint32_t* pmask = reinterpret_cast<uint32_t*>(recs + kRecs);    // producer-private [64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(pmask + kMaskWordsMax);
   uint64_t* q_full = bars;              // [2]
   uint64_t* q_empty = q_full + 2;       // [2]
   uint64_t* rec_full = q_empty + 2;     // [kRecs]
@@ -158,6 +173,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmap_q);
     tma_prefetch_desc(&tmap_k);
     tma_prefetch_desc(&tmap_v);
+    tma_prefetch_desc(&tmap_pk);
+    tma_prefetch_desc(&tmap_pv);
   }
   tc_fence_before();
   __syncthreads();
@@ -165,12 +182,107 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   WaitCtx wc{p.status, abort_flag, p.budget};
   const int bk_sub = a.block_k / 128;
+  const bool pool_tiles = a.corr && a.pooled_dt == DT;   // TMA pooled tiles vs gather
 
   if (warp == 0) {
     // ============================ producer ================================
-    int qcount = 0, icount = 0, kv = 0;
+    int qcount = 0, icount = 0, kv = 0, wstatic = blockIdx.x;
     bool ok = true;
-    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x) {
+    auto next_work = [&]() -> int {
+      int w = 0;
+      if (p.sched != nullptr) {
+        if (lane == 0) w = atomicAdd(p.sched, 1);
+        w = __shfl_sync(0xffffffffu, w, 0);
+      } else {
+        w = wstatic;
+        wstatic += gridDim.x;
+      }
+      return w;
+    };
+    // Publish one record; SEL/POOL/CORR records are followed by their K/V tiles.
+    auto emit = [&](const Rec& rec, const Chunk& ck, long long lrow) -> bool {
+      const int ri = icount % kRecs;
+      bool good = true;
+      if (lane == 0) good = mbar_wait(smem_u32(&rec_empty[ri]), ((icount / kRecs) & 1) ^ 1, wc);
+      good = __shfl_sync(0xffffffffu, good, 0);
+      if (!good) return false;
+      if (lane == 0) {
+        recs[ri] = rec;
+        mbar_arrive(smem_u32(&rec_full[ri]));
+      }
+      ++icount;
+      if (rec.kind == KIND_EMPTY || rec.kind == KIND_DONE) return true;
+      const int st = kv % kStages;
+      const uint32_t par = ((kv / kStages) & 1) ^ 1;
+      const uint32_t kst = k_smem + st * C::kTileBytes;
+      const uint32_t vst = v_smem + st * C::kTileBytes;
+      if (rec.kind != KIND_CORR) {
+        if (lane == 0) {
+          const CUtensorMap* mk = rec.kind == KIND_SEL ? &tmap_k : &tmap_pk;
+          const CUtensorMap* mv = rec.kind == KIND_SEL ? &tmap_v : &tmap_pv;
+          good = mbar_wait(smem_u32(&k_empty[st]), par, wc);
+          if (good) {
+            const uint32_t kb = smem_u32(&k_full[st]);
+            mbar_arrive_expect_tx(kb, (uint32_t)C::kTileBytes);
+#pragma unroll
+            for (int hh = 0; hh < C::kHalves; ++hh)
+              tma_load_3d(kst + hh * 16384, mk, kb, hh * 64, rec.kstart, ck.h);
+            good = mbar_wait(smem_u32(&v_empty[st]), par, wc);
+          }
+          if (good) {
+            const uint32_t vb = smem_u32(&v_full[st]);
+            mbar_arrive_expect_tx(vb, (uint32_t)C::kTileBytes);
+#pragma unroll
+            for (int hh = 0; hh < C::kHalves; ++hh)
+              tma_load_3d(vst + hh * 16384, mv, vb, hh * 64, rec.kstart, ck.h);
+          }
+        }
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) return false;
+      } else {
+        // Float32 pooled inputs: gather the listed rows, rounding to the compute dtype.
+        if (lane == 0) {
+          good = mbar_wait(smem_u32(&k_empty[st]), par, wc);
+          if (good) good = mbar_wait(smem_u32(&v_empty[st]), par, wc);
+        }
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) return false;
+        constexpr int kChunks = D / 8;   // 16-byte chunks per row
+        for (int idx = lane; idx < 128 * kChunks; idx += 32) {
+          const int e = idx / kChunks, cidx = idx % kChunks;
+          const int hh = cidx >> 3, cc = cidx & 7;
+          const uint32_t off = hh * 16384 + e * 128 + ((cc ^ (e & 7)) << 4);
+          uint4 kvk = make_uint4(0, 0, 0, 0), kvv = make_uint4(0, 0, 0, 0);
+          if (e < rec.nvalid) {
+            const int blk = clampi(a.pr_ids[lrow + rec.kstart + e], 0, a.Nb - 1);
+            const long long src = ((long long)ck.h * a.Nb + blk) * D + cidx * 8;
+            const float4* fk = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.pk) + src);
+            const float4* fv = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.pv) + src);
+            const float4 k0 = __ldg(fk), k1 = __ldg(fk + 1), v0 = __ldg(fv), v1 = __ldg(fv + 1);
+            kvk = make_uint4(pack2<DT>(k0.x, k0.y), pack2<DT>(k0.z, k0.w), pack2<DT>(k1.x, k1.y),
+                             pack2<DT>(k1.z, k1.w));
+            kvv = make_uint4(pack2<DT>(v0.x, v0.y), pack2<DT>(v0.z, v0.w), pack2<DT>(v1.x, v1.y),
+                             pack2<DT>(v1.z, v1.w));
+          }
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(kst + off), "r"(kvk.x),
+                       "r"(kvk.y), "r"(kvk.z), "r"(kvk.w)
+                       : "memory");
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(vst + off), "r"(kvv.x),
+                       "r"(kvv.y), "r"(kvv.z), "r"(kvv.w)
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(smem_u32(&k_full[st]));
+          mbar_arrive(smem_u32(&v_full[st]));
+        }
+      }
+      ++kv;
+      return true;
+    };
+
+    for (int w = next_work(); w < p.items && ok; w = next_work()) {
       const Chunk ck = make_chunk(p, w);
       const long long lrow = ((long long)ck.h * a.Nt + ck.t) * a.Nb;
       const int nsel = clampi(a.sel_counts[(long long)ck.h * a.Nt + ck.t], 0, a.Nb);
@@ -191,8 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ++qcount;
       }
-      // Count the KV items (the walk stops at the first block past the chunk,
-      // fpv2/kernel.py:249-255).
+      // Selected blocks up to the first one past the chunk (fpv2/kernel.py:249-255).
       int n_sel_items = 0, brk = nsel;
       for (int i0 = 0; i0 < nsel; i0 += 32) {
         const int i = i0 + lane;
@@ -208,94 +319,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         n_sel_items += contrib;
         if (stop) { brk = i0 + lim; break; }
       }
-      const int n_corr_items = (npr + 127) / 128;
+      // Pooled correction items.
+      int n_corr_items = 0;
+      const int n_ptiles = (a.Nb + 127) / 128;
+      if (pool_tiles && npr > 0) {
+        const int nwords = (a.Nb + 31) / 32;
+        for (int i = lane; i < nwords; i += 32) pmask[i] = 0u;
+        __syncwarp();
+        for (int i = lane; i < npr; i += 32) {
+          const int blk = clampi(a.pr_ids[lrow + i], 0, a.Nb - 1);
+          atomicOr(&pmask[blk >> 5], 1u << (blk & 31));
+        }
+        __syncwarp();
+        for (int j = 0; j < n_ptiles; ++j) {
+          const int w0 = 4 * j;
+          uint32_t any = 0;
+          for (int x = 0; x < 4 && w0 + x < nwords; ++x) any |= pmask[w0 + x];
+          n_corr_items += any != 0u;
+        }
+      } else if (npr > 0) {
+        n_corr_items = (npr + 127) / 128;
+      }
       const int n_items = max(1, n_sel_items + n_corr_items);
       int emitted = 0;
-
-      // Publish one record (and its K/V data) per item.
-      auto emit = [&](int kind, int kstart, int nvalid) -> bool {
-        const int ri = icount % kRecs;
-        bool good = true;
-        if (lane == 0) good = mbar_wait(smem_u32(&rec_empty[ri]), ((icount / kRecs) & 1) ^ 1, wc);
-        good = __shfl_sync(0xffffffffu, good, 0);
-        if (!good) return false;
-        if (lane == 0) {
-          recs[ri].kind = kind;
-          recs[ri].kstart = kstart;
-          recs[ri].nvalid = nvalid;
-          recs[ri].last = (emitted == n_items - 1) ? 1 : 0;
-          mbar_arrive(smem_u32(&rec_full[ri]));
-        }
-        ++icount;
+      auto make_rec = [&](int kind, int kstart, int nvalid) {
+        Rec r;
+        r.kind = kind;
+        r.kstart = kstart;
+        r.nvalid = nvalid;
+        r.flags = (emitted == 0 ? 1 : 0) | (emitted == n_items - 1 ? 2 : 0);
+        r.w = w;
+        r.mask[0] = r.mask[1] = r.mask[2] = r.mask[3] = 0u;
         ++emitted;
-        if (kind == KIND_EMPTY) return true;
-        const int st = kv % kStages;
-        const uint32_t par = ((kv / kStages) & 1) ^ 1;
-        if (lane == 0) {
-          good = mbar_wait(smem_u32(&k_empty[st]), par, wc);
-          if (good) good = mbar_wait(smem_u32(&v_empty[st]), par, wc);
-        }
-        good = __shfl_sync(0xffffffffu, good, 0);
-        if (!good) return false;
-        const uint32_t kst = k_smem + st * C::kTileBytes;
-        const uint32_t vst = v_smem + st * C::kTileBytes;
-        if (kind == KIND_SEL) {
-          if (lane == 0) {
-            const uint32_t kb = smem_u32(&k_full[st]);
-            mbar_arrive_expect_tx(kb, (uint32_t)C::kTileBytes);
-#pragma unroll
-            for (int hh = 0; hh < C::kHalves; ++hh)
-              tma_load_3d(kst + hh * 16384, &tmap_k, kb, hh * 64, kstart, ck.h);
-            const uint32_t vb = smem_u32(&v_full[st]);
-            mbar_arrive_expect_tx(vb, (uint32_t)C::kTileBytes);
-#pragma unroll
-            for (int hh = 0; hh < C::kHalves; ++hh)
-              tma_load_3d(vst + hh * 16384, &tmap_v, vb, hh * 64, kstart, ck.h);
-          }
-        } else {
-          // Gather pooled rows into the swizzled K and V tiles.
-          constexpr int kChunks = D / 8;   // 16-byte chunks per row
-          for (int idx = lane; idx < 128 * kChunks; idx += 32) {
-            const int e = idx / kChunks, cidx = idx % kChunks;
-            const int hh = cidx >> 3, cc = cidx & 7;
-            const uint32_t off = hh * 16384 + e * 128 + ((cc ^ (e & 7)) << 4);
-            uint4 kvk = make_uint4(0, 0, 0, 0), kvv = make_uint4(0, 0, 0, 0);
-            if (e < nvalid) {
-              const int blk = clampi(a.pr_ids[lrow + kstart + e], 0, a.Nb - 1);
-              const long long src = ((long long)ck.h * a.Nb + blk) * D + cidx * 8;
-              if (a.pooled_dt == DT) {
-                kvk = __ldg(reinterpret_cast<const uint4*>(
-                    reinterpret_cast<const typename Elem<DT>::T*>(a.pk) + src));
-                kvv = __ldg(reinterpret_cast<const uint4*>(
-                    reinterpret_cast<const typename Elem<DT>::T*>(a.pv) + src));
-              } else {   // float32 pooled: round to the compute dtype
-                const float4* fk = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.pk) + src);
-                const float4* fv = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.pv) + src);
-                const float4 k0 = __ldg(fk), k1 = __ldg(fk + 1), v0 = __ldg(fv), v1 = __ldg(fv + 1);
-                kvk = make_uint4(pack2<DT>(k0.x, k0.y), pack2<DT>(k0.z, k0.w), pack2<DT>(k1.x, k1.y),
-                                 pack2<DT>(k1.z, k1.w));
-                kvv = make_uint4(pack2<DT>(v0.x, v0.y), pack2<DT>(v0.z, v0.w), pack2<DT>(v1.x, v1.y),
-                                 pack2<DT>(v1.z, v1.w));
-              }
-            }
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(kst + off), "r"(kvk.x),
-                         "r"(kvk.y), "r"(kvk.z), "r"(kvk.w)
-                         : "memory");
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(vst + off), "r"(kvv.x),
-                         "r"(kvv.y), "r"(kvv.z), "r"(kvv.w)
-                         : "memory");
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(smem_u32(&k_full[st]));
-            mbar_arrive(smem_u32(&v_full[st]));
-          }
-        }
-        ++kv;
-        return true;
+        return r;
       };
-
       for (int i0 = 0; i0 < brk && ok; i0 += 32) {
         const int i = i0 + lane;
         const int blk = i < brk ? clampi(a.sel_ids[lrow + i], 0, a.Nb - 1) : 0;
@@ -306,13 +363,41 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int sub = 0; sub < bk_sub && ok; ++sub) {
             const long long ks = bstart + sub * 128;
             if (ks > ck.abs_last) break;
-            ok = emit(KIND_SEL, (int)ks, 0);
+            ok = emit(make_rec(KIND_SEL, (int)ks, 0), ck, lrow);
           }
         }
       }
-      for (int j = 0; j < n_corr_items && ok; ++j)
-        ok = emit(KIND_CORR, j * 128, min(128, npr - j * 128));
-      if (ok && n_sel_items + n_corr_items == 0) ok = emit(KIND_EMPTY, 0, 0);
+      if (pool_tiles) {
+        const int nwords = (a.Nb + 31) / 32;
+        for (int j = 0; j < n_ptiles && ok && npr > 0; ++j) {
+          uint32_t m4[4];
+          uint32_t any = 0;
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            m4[x] = (4 * j + x < nwords) ? pmask[4 * j + x] : 0u;
+            any |= m4[x];
+          }
+          if (!any) continue;
+          Rec r = make_rec(KIND_POOL, j * 128, 0);
+#pragma unroll
+          for (int x = 0; x < 4; ++x) r.mask[x] = m4[x];
+          ok = emit(r, ck, lrow);
+        }
+        __syncwarp();   // pmask reads done before the next work item clears it
+      } else {
+        for (int j = 0; j < n_corr_items && ok; ++j)
+          ok = emit(make_rec(KIND_CORR, j * 128, min(128, npr - j * 128)), ck, lrow);
+      }
+      if (ok && n_sel_items + n_corr_items == 0) ok = emit(make_rec(KIND_EMPTY, 0, 0), ck, lrow);
+    }
+    if (ok) {
+      Rec done;
+      done.kind = KIND_DONE;
+      done.kstart = done.nvalid = done.w = 0;
+      done.flags = 3;
+      done.mask[0] = done.mask[1] = done.mask[2] = done.mask[3] = 0u;
+      Chunk none{};
+      emit(done, none, 0);
     }
     // Drain in-flight bulk copies before the CTA retires.
     if (lane == 0) {
@@ -331,80 +416,86 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ============================ MMA issuer ==============================
     if (lane == 0) {
-      int qcount = 0, icount = 0, kv = 0, wi = 0;
-      bool ok = true;
-      for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++wi) {
-        const int qs = qcount & 1;
-        ok = mbar_wait(smem_u32(&q_full[qs]), (qcount >> 1) & 1, wc);
-        if (!ok) break;
-        ++qcount;
-        bool need_ofree = wi > 0;
-        bool first_pv = true;
-        int prev = -1;   // kv index whose PV is pending
-        auto issue_pv = [&](int n) -> bool {
-          const int st = n % kStages;
-          const uint32_t par = (n / kStages) & 1;
-          if (!mbar_wait(smem_u32(&p_full[st]), par, wc)) return false;
-          if (!mbar_wait(smem_u32(&v_full[st]), par, wc)) return false;
-          if (need_ofree) {
-            if (!mbar_wait(smem_u32(o_free), (wi - 1) & 1, wc)) return false;
-            need_ofree = false;
-          }
-          tc_fence_after();
-          const uint32_t o_tmem = tmem_base + C::kOCol;
-          const uint32_t p_tmem = tmem_base + C::kSCol + st * 128;
-          const uint32_t vst = v_smem + st * C::kTileBytes;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t bdesc = sw128_desc(vst + kk * 2048, 16384, 1024);
-            umma_ts(o_tmem, p_tmem + kk * 8, bdesc, p.idesc_pv, (first_pv && kk == 0) ? 0u : 1u);
-          }
-          first_pv = false;
-          umma_commit(smem_u32(&v_empty[st]));
-          umma_commit(smem_u32(&s_free[st]));
-          umma_commit(smem_u32(pv_done));
-          return true;
-        };
-        while (ok) {
-          const int ri = icount % kRecs;
-          ok = mbar_wait(smem_u32(&rec_full[ri]), (icount / kRecs) & 1, wc);
-          if (!ok) break;
-          const Rec rec = recs[ri];
-          mbar_arrive(smem_u32(&rec_empty[ri]));
-          ++icount;
-          if (rec.kind != KIND_EMPTY) {
-            const int st = kv % kStages;
-            const uint32_t par = (kv / kStages) & 1;
-            ok = mbar_wait(smem_u32(&k_full[st]), par, wc);
-            if (ok) ok = mbar_wait(smem_u32(&s_free[st]), par ^ 1, wc);
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t s_tmem = tmem_base + C::kSCol + st * 128;
-            const uint32_t qb = q_smem + qs * C::kTileBytes;
-            const uint32_t kb = k_smem + st * C::kTileBytes;
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const int hh = kk / 4, sub = kk % 4;
-              const uint64_t adesc = sw128_desc(qb + hh * 16384 + sub * 32, 16, 1024);
-              const uint64_t bdesc = sw128_desc(kb + hh * 16384 + sub * 32, 16, 1024);
-              umma_ss(s_tmem, adesc, bdesc, p.idesc_qk, kk > 0 ? 1u : 0u);
-            }
-            umma_commit(smem_u32(&s_full[st]));
-            umma_commit(smem_u32(&k_empty[st]));
-            if (prev >= 0) ok = issue_pv(prev);
-            prev = kv;
-            ++kv;
-          }
-          if (rec.last) break;
-        }
-        if (ok && prev >= 0) ok = issue_pv(prev);
-        if (!ok) break;
-        umma_commit(smem_u32(&q_empty[qs]));
+      int qcount = 0, icount = 0, kv = 0, wi = 0, qs = 0;
+      bool ok = true, need_ofree = false, first_pv = true;
+      int prev = -1;   // kv index whose PV is pending
+      auto issue_pv = [&](int n) -> bool {
+        const int st = n % kStages;
+        const uint32_t par = (n / kStages) & 1;
+        if (!mbar_wait(smem_u32(&p_full[st]), par, wc)) return false;
+        if (!mbar_wait(smem_u32(&v_full[st]), par, wc)) return false;
         if (need_ofree) {
-          ok = mbar_wait(smem_u32(o_free), (wi - 1) & 1, wc);
+          if (!mbar_wait(smem_u32(o_free), (wi - 1) & 1, wc)) return false;
           need_ofree = false;
         }
-        umma_commit(smem_u32(o_full));
+        tc_fence_after();
+        const uint32_t o_tmem = tmem_base + C::kOCol;
+        const uint32_t p_tmem = tmem_base + C::kSCol + st * 128;
+        const uint32_t vst = v_smem + st * C::kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t bdesc = sw128_desc(vst + kk * 2048, 16384, 1024);
+          umma_ts(o_tmem, p_tmem + kk * 8, bdesc, p.idesc_pv, (first_pv && kk == 0) ? 0u : 1u);
+        }
+        first_pv = false;
+        umma_commit(smem_u32(&v_empty[st]));
+        umma_commit(smem_u32(&s_free[st]));
+        umma_commit(smem_u32(pv_done));
+        return true;
+      };
+      while (ok) {
+        const int ri = icount % kRecs;
+        ok = mbar_wait(smem_u32(&rec_full[ri]), (icount / kRecs) & 1, wc);
+        if (!ok) break;
+        const Rec rec = recs[ri];
+        mbar_arrive(smem_u32(&rec_empty[ri]));
+        ++icount;
+        if (rec.kind == KIND_DONE) break;
+        if (rec.flags & 1) {   // first item of a work item
+          qs = qcount & 1;
+          ok = mbar_wait(smem_u32(&q_full[qs]), (qcount >> 1) & 1, wc);
+          if (!ok) break;
+          ++qcount;
+          need_ofree = wi > 0;
+          first_pv = true;
+          prev = -1;
+        }
+        if (rec.kind != KIND_EMPTY) {
+          const int st = kv % kStages;
+          const uint32_t par = (kv / kStages) & 1;
+          ok = mbar_wait(smem_u32(&k_full[st]), par, wc);
+          if (ok) ok = mbar_wait(smem_u32(&s_free[st]), par ^ 1, wc);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t s_tmem = tmem_base + C::kSCol + st * 128;
+          const uint32_t qb = q_smem + qs * C::kTileBytes;
+          const uint32_t kb = k_smem + st * C::kTileBytes;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int hh = kk / 4, sub = kk % 4;
+            const uint64_t adesc = sw128_desc(qb + hh * 16384 + sub * 32, 16, 1024);
+            const uint64_t bdesc = sw128_desc(kb + hh * 16384 + sub * 32, 16, 1024);
+            umma_ss(s_tmem, adesc, bdesc, p.idesc_qk, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(smem_u32(&s_full[st]));
+          umma_commit(smem_u32(&k_empty[st]));
+          if (prev >= 0) ok = issue_pv(prev);
+          if (!ok) break;
+          prev = kv;
+          ++kv;
+        }
+        if (rec.flags & 2) {   // last item: finish the work item
+          if (prev >= 0) ok = issue_pv(prev);
+          if (!ok) break;
+          prev = -1;
+          umma_commit(smem_u32(&q_empty[qs]));
+          if (need_ofree) {
+            ok = mbar_wait(smem_u32(o_free), (wi - 1) & 1, wc);
+            need_ofree = false;
+          }
+          umma_commit(smem_u32(o_full));
+          ++wi;
+        }
       }
       umma_commit(smem_u32(drain));
       mbar_wait(smem_u32(drain), 0, wc, false);
@@ -417,26 +508,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float c2 = a.scale_log2;
     int icount = 0, kv = 0, wi = 0;
     bool ok = true;
-    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++wi) {
-      const Chunk ck = make_chunk(p, w);
-      const int P = ck.c * 128 + r;
-      const int gq = P / a.tile_q;
-      const int pos = P % a.tile_q;
-      const long long row = (long long)ck.t * a.tile_q + pos;
-      const long long position = (long long)a.offset + row;
-      const bool row_valid = row < a.valid_lq;
-      float m_used = kFiniteMin, l = 0.f;
-      int pv_wi = 0;
-      while (true) {
-        const int ri = icount % kRecs;
-        ok = mbar_wait(smem_u32(&rec_full[ri]), (icount / kRecs) & 1, wc);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-        const Rec rec = recs[ri];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&rec_empty[ri]));
-        ++icount;
-        if (rec.kind == KIND_EMPTY) break;
+    // Per work item state.
+    Chunk ck{};
+    int gq = 0;
+    long long row = 0, position = 0;
+    bool row_valid = false;
+    float m_used = kFiniteMin, l = 0.f;
+    int pv_wi = 0;
+    while (ok) {
+      const int ri = icount % kRecs;
+      ok = mbar_wait(smem_u32(&rec_full[ri]), (icount / kRecs) & 1, wc);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      const Rec rec = recs[ri];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&rec_empty[ri]));
+      ++icount;
+      if (rec.kind == KIND_DONE) break;
+      if (rec.flags & 1) {
+        ck = make_chunk(p, rec.w);
+        const int P = ck.c * 128 + r;
+        gq = P / a.tile_q;
+        row = (long long)ck.t * a.tile_q + P % a.tile_q;
+        position = (long long)a.offset + row;
+        row_valid = row < a.valid_lq;
+        m_used = kFiniteMin;
+        l = 0.f;
+        pv_wi = 0;
+      }
+      if (rec.kind != KIND_EMPTY) {
         const int st = kv % kStages;
         const uint32_t par = (kv / kStages) & 1;
         ok = mbar_wait(smem_u32(&s_full[st]), par, wc);
@@ -450,30 +550,62 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) reg_fence(s[q4]);
-        float x[4][32];
-        float mt = kFiniteMin;
+        // x = logit (base 2) of each key/entry; masked -> finite_min.
+        float bias = 0.f;
+        bool full;
+        uint32_t vmask[4];
         if (rec.kind == KIND_SEL) {
           const long long ks = rec.kstart;
-          const bool full = row_valid && ks + 127 <= position && ks + 127 < a.valid_lk;
+          full = row_valid && ks + 127 <= position && ks + 127 < a.valid_lk;
+          if (!full) {
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4)
+            for (int q4 = 0; q4 < 4; ++q4) {
+              uint32_t m = 0u;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const long long key = ks + q4 * 32 + j;
-              const bool v = full || (row_valid && key <= position && key < a.valid_lk);
-              x[q4][j] = v ? __uint_as_float(s[q4][j]) * c2 : kFiniteMin;
-              mt = fmaxf(mt, x[q4][j]);
+              for (int j = 0; j < 32; ++j) {
+                const long long key = ks + q4 * 32 + j;
+                m |= (row_valid && key <= position && key < a.valid_lk) ? (1u << j) : 0u;
+              }
+              vmask[q4] = m;
             }
+          }
+        } else if (rec.kind == KIND_POOL) {
+          bias = a.corr_shift;
+          full = false;
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) vmask[q4] = rec.mask[q4];
+        } else {   // KIND_CORR
+          bias = a.corr_shift;
+          full = rec.nvalid >= 128;
+          if (!full) {
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              const int nv = rec.nvalid - q4 * 32;
+              vmask[q4] = nv >= 32 ? 0xffffffffu : (nv <= 0 ? 0u : ((1u << nv) - 1u));
+            }
+          }
+        }
+        // Row max over valid entries (raw scores; c2 > 0 so the order is kept).
+        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            mx0 = fmaxf(mx0, __uint_as_float(s[0][j]));
+            mx1 = fmaxf(mx1, __uint_as_float(s[1][j]));
+            mx2 = fmaxf(mx2, __uint_as_float(s[2][j]));
+            mx3 = fmaxf(mx3, __uint_as_float(s[3][j]));
+          }
         } else {
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4)
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const bool v = q4 * 32 + j < rec.nvalid;
-              x[q4][j] = v ? fmaf(__uint_as_float(s[q4][j]), c2, a.corr_shift) : kFiniteMin;
-              mt = fmaxf(mt, x[q4][j]);
-            }
+          for (int j = 0; j < 32; ++j) {
+            if ((vmask[0] >> j) & 1u) mx0 = fmaxf(mx0, __uint_as_float(s[0][j]));
+            if ((vmask[1] >> j) & 1u) mx1 = fmaxf(mx1, __uint_as_float(s[1][j]));
+            if ((vmask[2] >> j) & 1u) mx2 = fmaxf(mx2, __uint_as_float(s[2][j]));
+            if ((vmask[3] >> j) & 1u) mx3 = fmaxf(mx3, __uint_as_float(s[3][j]));
+          }
         }
+        const float mraw = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        const float mt = mraw == -INFINITY ? kFiniteMin : fmaf(mraw, c2, bias);
         const float m_new = fmaxf(m_used, mt);
         const bool need = m_new > m_used + kRescaleThreshold ||
                           (m_used == kFiniteMin && m_new > kFiniteMin);
@@ -503,18 +635,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_wait_st();
           }
         }
-        float rs = 0.f;
+        // P = 2^(s*c2 + bias - m); a masked entry weighs 2^(finite_min - m), i.e.
+        // 1 while the row has seen nothing but masked entries, else 0.
+        const float neg_m = bias - m_used;
+        const float masked_p = (m_used == kFiniteMin) ? 1.f : 0.f;
+        float rs0 = 0.f, rs1 = 0.f, rs2 = 0.f, rs3 = 0.f;
         uint32_t pk[2][32];
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
+        for (int q4 = 0; q4 < 4; ++q4) {
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            const float p0 = ex2(x[q4][j] - m_used);
-            const float p1 = ex2(x[q4][j + 1] - m_used);
-            rs += p0 + p1;
+            float p0 = ex2(fmaf(__uint_as_float(s[q4][j]), c2, neg_m));
+            float p1 = ex2(fmaf(__uint_as_float(s[q4][j + 1]), c2, neg_m));
+            if (!full) {
+              if (!((vmask[q4] >> j) & 1u)) p0 = masked_p;
+              if (!((vmask[q4] >> (j + 1)) & 1u)) p1 = masked_p;
+            }
+            if (q4 == 0) rs0 += p0 + p1;
+            else if (q4 == 1) rs1 += p0 + p1;
+            else if (q4 == 2) rs2 += p0 + p1;
+            else rs3 += p0 + p1;
             pk[q4 >> 1][(q4 & 1) * 16 + (j >> 1)] = pack2<DT>(p0, p1);
           }
-        l += rs;
+        }
+        l += (rs0 + rs1) + (rs2 + rs3);
         tmem_st32(s_tmem, pk[0]);
         tmem_st32(s_tmem + 32, pk[1]);
         tmem_wait_st();
@@ -523,41 +667,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(smem_u32(&p_full[st]));
         ++kv;
         ++pv_wi;
-        if (rec.last) break;
       }
-      if (!ok) break;
-      // ---- epilogue: O / l -> out ------------------------------------------
-      ok = mbar_wait(smem_u32(o_full), wi & 1, wc);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
-      using T = typename Elem<DT>::T;
-      T* out = reinterpret_cast<T*>(a.out) +
-               (((long long)(ck.h * a.G + gq)) * a.Lq_pad + row) * D;
-      const float inv = pv_wi > 0 ? 1.f / l : 0.f;
+      if (rec.flags & 2) {
+        // ---- epilogue: O / l -> out ----------------------------------------
+        ok = mbar_wait(smem_u32(o_full), wi & 1, wc);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        using T = typename Elem<DT>::T;
+        T* out = reinterpret_cast<T*>(a.out) +
+                 (((long long)(ck.h * a.G + gq)) * a.Lq_pad + row) * D;
+        const float inv = pv_wi > 0 ? 1.f / l : 0.f;
 #pragma unroll
-      for (int dc = 0; dc < D / 32; ++dc) {
-        uint32_t o[32];
-        if (pv_wi > 0) {
-          tmem_ld32(tmem_base + lane_off + C::kOCol + dc * 32, o);
-          tmem_wait_ld();
-          reg_fence(o);
-        } else {
+        for (int dc = 0; dc < D / 32; ++dc) {
+          uint32_t o[32];
+          if (pv_wi > 0) {
+            tmem_ld32(tmem_base + lane_off + C::kOCol + dc * 32, o);
+            tmem_wait_ld();
+            reg_fence(o);
+          } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] = 0u;
+            for (int j = 0; j < 32; ++j) o[j] = 0u;
+          }
+          uint32_t packed[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            packed[j] = pack2<DT>(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
+          uint4* dst = reinterpret_cast<uint4*>(out + dc * 32);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
         }
-        uint32_t packed[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          packed[j] = pack2<DT>(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
-        uint4* dst = reinterpret_cast<uint4*>(out + dc * 32);
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(o_free));
+        ++wi;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(o_free));
     }
   }
 
@@ -570,7 +715,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int D>
 size_t smem_bytes() {
   return 1024 + (size_t)(2 + 2 * kStages) * Cfg<D>::kTileBytes + sizeof(Rec) * kRecs +
-         8 * (4 + 2 * kRecs + 7 * kStages + 4) + 16;
+         4 * kMaskWordsMax + 8 * (4 + 2 * kRecs + 7 * kStages + 4) + 16;
 }
 
 }  // namespace
@@ -580,13 +725,15 @@ bool attn_tc_supported(const AttnArgs& a) {
   if (a.D != 64 && a.D != 128) return false;
   if (a.pooled_dt != a.dt && a.pooled_dt != DT_F32) return false;
   if (a.block_k % 128 != 0) return false;
+  if (!(a.scale_log2 > 0.f)) return false;
+  if (a.Nb > 32 * kMaskWordsMax) return false;
   const int R = a.G * a.tile_q;
   if (R % 128 != 0) return false;
   if (a.tile_q % 128 != 0 && 128 % a.tile_q != 0) return false;
   return true;
 }
 
-cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, cudaStream_t stream) {
+cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, int* sched, cudaStream_t stream) {
   Params p;
   p.a = a;
   p.nch = (a.G * a.tile_q) / 128;
@@ -594,26 +741,39 @@ cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, cudaStream_t st
   const int fmt = a.dt == DT_BF16 ? 1 : 0;
   p.idesc_qk = umma_idesc_f16(fmt, 128, 128, 0, 0);
   p.idesc_pv = umma_idesc_f16(fmt, 128, a.D, 0, 1);
+  p.sched = sched;
   p.status = L.status;
   p.budget = L.budget;
   if (p.items == 0) return cudaSuccess;
 
   const int box_rows = a.tile_q >= 128 ? 128 : a.tile_q;
   const int box_heads = 128 / box_rows;
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, tpk, tpv;
   if (!encode_tmap_3d(&tq, a.q, a.dt, a.D, a.Lq_pad, a.Hq, 64, box_rows, box_heads))
     return cudaErrorInvalidValue;
   if (!encode_tmap_3d(&tk, a.k, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return cudaErrorInvalidValue;
   if (!encode_tmap_3d(&tv, a.v, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return cudaErrorInvalidValue;
+  // Pooled tiles (only read when pooled K/V share the compute dtype).
+  const bool pooled_ok = a.corr && a.pooled_dt == a.dt;
+  if (!encode_tmap_3d(&tpk, pooled_ok ? a.pk : a.k, a.dt, a.D, pooled_ok ? a.Nb : a.Lk_pad, a.Hkv,
+                      64, 128, 1))
+    return cudaErrorInvalidValue;
+  if (!encode_tmap_3d(&tpv, pooled_ok ? a.pv : a.v, a.dt, a.D, pooled_ok ? a.Nb : a.Lk_pad, a.Hkv,
+                      64, 128, 1))
+    return cudaErrorInvalidValue;
   const int grid = max(1, min(L.num_sms, p.items));
   cudaError_t e = cudaSuccess;
+  if (sched != nullptr) {
+    e = cudaMemsetAsync(sched, 0, sizeof(int), stream);
+    if (e != cudaSuccess) return e;
+  }
 #define FPV2_ATTN_LAUNCH(DD, TT)                                                            \
   {                                                                                         \
     const size_t smem = smem_bytes<DD>();                                                   \
     e = cudaFuncSetAttribute(attn_tc_kernel<DD, TT>,                                        \
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
     if (e != cudaSuccess) return e;                                                         \
-    attn_tc_kernel<DD, TT><<<grid, kThreads, smem, stream>>>(tq, tk, tv, p);                \
+    attn_tc_kernel<DD, TT><<<grid, kThreads, smem, stream>>>(tq, tk, tv, tpk, tpv, p);      \
   }
   if (a.D == 64 && a.dt == DT_BF16) FPV2_ATTN_LAUNCH(64, DT_BF16)
   else if (a.D == 64 && a.dt == DT_F16) FPV2_ATTN_LAUNCH(64, DT_F16)

@@ -397,7 +397,8 @@ int fpv2_sparse_attention(const void* q, const void* k, const void* v, const voi
                           int32_t padded_k_len, int32_t head_dim, int32_t offset,
                           int32_t query_length, int32_t key_length, float scale,
                           int32_t block_k, int32_t tile_q, int32_t mean_correction,
-                          void* out, void* stream) {
+                          void* out, void* workspace, int64_t workspace_bytes,
+                          void* stream) {
   if (dtype != DT_F16 && dtype != DT_BF16)
     return fail(FPV2_ERR_INVALID_ARGUMENT, "q, k, and v must share float16 or bfloat16 dtype");
   if (pooled_dtype != dtype && pooled_dtype != DT_F32)
@@ -459,7 +460,10 @@ int fpv2_sparse_attention(const void* q, const void* k, const void* v, const voi
                                     reinterpret_cast<uintptr_t>(pooled_v) % 16 == 0));
   cudaError_t e;
   if (aligned && attn_tc_supported(a)) {
-    e = launch_attn_tc(a, tc_launch(*d), s);
+    int* sched = (workspace != nullptr && workspace_bytes >= (int64_t)sizeof(int))
+                     ? reinterpret_cast<int*>(workspace)
+                     : nullptr;
+    e = launch_attn_tc(a, tc_launch(*d), sched, s);
     if (e != cudaSuccess) return cuda_fail(e, "attn_tc launch");
   } else {
     e = launch_attn_generic(a, s);
@@ -486,6 +490,8 @@ int fpv2_fast_path_mask(int dtype, int32_t q_heads, int32_t kv_heads, int32_t he
   a.G = g.G;
   a.block_k = block_k;
   a.tile_q = tile_q;
+  a.Nb = num_blocks;
+  a.scale_log2 = 1.f;   // any positive softmax scale
   int m = 0;
   if (select_tc_supported(g, dtype)) m |= 1;
   if (attn_tc_supported(a)) m |= 2;

@@ -92,8 +92,10 @@ cudaError_t launch_select_tc(const SelectTcArgs& a, const void* q, const void* p
                              const TcLaunch& L, cudaStream_t stream);
 
 // attn_tc.cu: FlashAttention-style block-sparse attention on tensor cores.
+// `sched` (nullable) is one int of device scratch used as the work-queue
+// counter; it is zeroed on `stream` before the launch. Null = static schedule.
 bool attn_tc_supported(const AttnArgs& a);
-cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, cudaStream_t stream);
+cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, int* sched, cudaStream_t stream);
 
 // selftest.cu: bounded-wait failure detection.
 cudaError_t launch_wait_selftest(const TcLaunch& L, cudaStream_t stream);

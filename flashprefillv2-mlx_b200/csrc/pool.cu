@@ -42,11 +42,22 @@ __global__ void __launch_bounds__(kPoolThreads)
 #pragma unroll
   for (int i = 0; i < kPerVec; ++i) acc[i] = 0.0;
   if (rsub < rows_in_flight) {
-    for (int r = rsub; r < a.bs; r += rows_in_flight) {
-      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)r * a.D));
-      const Tin* e = reinterpret_cast<const Tin*>(&raw);
+    // Issue 8 independent 16-byte loads before accumulating (memory-level parallelism).
+    constexpr int kBatch = 8;
+    for (int r0 = rsub; r0 < a.bs; r0 += kBatch * rows_in_flight) {
+      uint4 raw[kBatch];
 #pragma unroll
-      for (int i = 0; i < kPerVec; ++i) acc[i] += (double)Elem<DT_IN>::to_f(e[i]);
+      for (int u = 0; u < kBatch; ++u) {
+        const int r = r0 + u * rows_in_flight;
+        raw[u] = r < a.bs ? __ldg(reinterpret_cast<const uint4*>(base + (int64_t)r * a.D))
+                          : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const Tin* e = reinterpret_cast<const Tin*>(&raw[u]);
+#pragma unroll
+        for (int i = 0; i < kPerVec; ++i) acc[i] += (double)Elem<DT_IN>::to_f(e[i]);
+      }
     }
   }
   // Reduce the row groups: [rows_in_flight][D] partial sums in shared memory.

@@ -84,6 +84,21 @@ __device__ __forceinline__ Item make_item(const Params& p, int w) {
   return it;
 }
 
+// Order-preserving float <-> uint32 encoding (for atomicMax on floats).
+__device__ __forceinline__ uint32_t f2ord(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float ord2f(uint32_t o) {
+  return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+}
+
+__device__ __forceinline__ float lg2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -122,8 +137,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = t_empty + kTmemSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* red = reinterpret_cast<float*>(tmem_slot + 2);   // [8]
-  int* totals = reinterpret_cast<int*>(red + 8);          // [2]
+  uint32_t* sred = tmem_slot + 2;                          // [2] ordered-int M, K
+  int* totals = reinterpret_cast<int*>(sred + 2);          // [2]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -262,16 +277,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ======================= energy + finalize =============================
+    // Thread (quarter, lane) owns block b = 128 m + 32 quarter + lane of every
+    // M-tile m: m_b = max over the tile's visible rows of x = s * log2(e), and
+    // e_b = sum_rows 2^(x - m_b). The tile max M = max_b m_b and the energy max
+    // 2^(K - M) with K = max_b (m_b + log2 e_b) are reduced with shared-memory
+    // atomics on order-preserving integer encodings while the tiles stream by.
     const int et = threadIdx.x - 64;           // 0..127
     const int quarter = warp & 3;              // TMEM lane group of this warp
     const int ew = et >> 5;                    // 0..3 index among energy warps
     const unsigned lt = (1u << lane) - 1u;
+    const float c = p.scale_log2;              // > 0 on this path
     int tcount = 0;
     bool ok = true;   // after a failed wait the role keeps its barrier schedule but skips TMEM
+    if (et == 0) {
+      sred[0] = f2ord(-INFINITY);
+      sred[1] = f2ord(-INFINITY);
+    }
+    named_bar_sync(1, 128);
     for (int w = blockIdx.x; w < total_work; w += gridDim.x) {
       const Item it = make_item(p, w);
       const long long row_base = ((long long)it.h * g.Nt + it.t) * Nb;
-      for (int c = 0; c < p.n_chunks; ++c) {
+      for (int cc = 0; cc < p.n_chunks; ++cc) {
         for (int m = 0; m < it.n_mt; ++m) {
           const int ts = tcount % kTmemSlots;
           if (ok) ok = mbar_wait(smem_u32(&t_full[ts]), (tcount / kTmemSlots) & 1, wc);
@@ -280,42 +306,79 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const int b = m * 128 + quarter * 32 + lane;
           if (ok && m * 128 + quarter * 32 < it.n_full) {
+            const bool bvalid = b < it.n_full;
             float mb = -INFINITY, eb = 0.f;
-            if (c > 0 && b < it.n_full) {
+            if (cc > 0 && bvalid) {
               const float2 st = stats[b];
               mb = st.x;
               eb = st.y;
             }
-            const long long bstart = (long long)b * g.block_k;
-            const bool bvalid = b < it.n_full;
-            for (int col0 = 0; col0 < p.NC; col0 += 32) {
-              uint32_t r[32];
-              tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + ts * 128 + col0, r);
-              tmem_wait_ld();
-              reg_fence(r);
-              float x[32];
-              float cmax = -INFINITY;
+            uint32_t sv[4][32];
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + ts * 128;
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4)
+              if (q4 * 32 < p.NC) tmem_ld32(taddr + q4 * 32, sv[q4]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) reg_fence(sv[q4]);
+            const uint32_t kNegInf = 0xff800000u;
+            if (!bvalid || it.row_mask) {
+              const long long bstart = (long long)b * g.block_k;
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4)
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  const int col = q4 * 32 + j;
+                  bool v = bvalid && col < p.NC;
+                  if (v && it.row_mask) {
+                    const int P = cc * p.NC + col;
+                    const long long row = (long long)it.t * g.tile_q + P % g.tile_q;
+                    v = row < g.valid_lq && bstart <= g.offset + row;
+                  }
+                  if (!v) sv[q4][j] = kNegInf;
+                }
+            } else if (p.NC < 128) {
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4)
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (q4 * 32 + j >= p.NC) sv[q4][j] = kNegInf;
+            }
+            float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              m0 = fmaxf(m0, __uint_as_float(sv[0][j]));
+              m1 = fmaxf(m1, __uint_as_float(sv[1][j]));
+              m2 = fmaxf(m2, __uint_as_float(sv[2][j]));
+              m3 = fmaxf(m3, __uint_as_float(sv[3][j]));
+            }
+            const float mraw = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+            const float mnew = fmaxf(mb, mraw * c);
+            if (mnew != -INFINITY) {
+              const float nm = -mnew;
+              float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
-                bool v = bvalid;
-                if (it.row_mask) {
-                  const int P = c * p.NC + col0 + j;
-                  const long long row = (long long)it.t * g.tile_q + P % g.tile_q;
-                  v = v && row < g.valid_lq && bstart <= g.offset + row;
-                }
-                x[j] = v ? __uint_as_float(r[j]) * p.scale_log2 : -INFINITY;
-                cmax = fmaxf(cmax, x[j]);
+                e0 += ex2(fmaf(__uint_as_float(sv[0][j]), c, nm));
+                e1 += ex2(fmaf(__uint_as_float(sv[1][j]), c, nm));
+                e2 += ex2(fmaf(__uint_as_float(sv[2][j]), c, nm));
+                e3 += ex2(fmaf(__uint_as_float(sv[3][j]), c, nm));
               }
-              const float mnew = fmaxf(mb, cmax);
-              if (mnew != -INFINITY) {
-                float acc = 0.f;
-#pragma unroll
-                for (int j = 0; j < 32; ++j) acc += ex2(x[j] - mnew);
-                eb = eb * ex2(mb - mnew) + acc;
-                mb = mnew;
-              }
+              eb = eb * ex2(mb - mnew) + ((e0 + e1) + (e2 + e3));
+              mb = mnew;
             }
             if (bvalid) stats[b] = make_float2(mb, eb);
+            if (cc == p.n_chunks - 1) {
+              // fold this block into the tile max M and the energy-max key K
+              float wm = bvalid ? mb : -INFINITY;
+              float wk = (bvalid && eb > 0.f) ? mb + lg2(eb) : -INFINITY;
+              wm = warp_max(wm);
+              wk = warp_max(wk);
+              if (lane == 0) {
+                atomicMax(&sred[0], f2ord(wm));
+                atomicMax(&sred[1], f2ord(wk));
+              }
+            }
           }
           tc_fence_before();
           __syncwarp();
@@ -323,32 +386,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
 
-      // ---- finalize: tile max, energies, threshold, forcing, lists --------
-      named_bar_sync(1, 128);
-      float lm = -INFINITY;
-      for (int b = et; b < it.n_full; b += 128) lm = fmaxf(lm, stats[b].x);
-      lm = warp_max(lm);
-      if (lane == 0) red[ew] = lm;
-      named_bar_sync(1, 128);
-      const float Mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-      float le = 0.f;
-      for (int b = et; b < it.n_full; b += 128) {
-        const float2 st = stats[b];
-        const float E = (Mx == -INFINITY || st.x == -INFINITY) ? 0.f : st.y * ex2(st.x - Mx);
-        stats[b].y = E;
-        le = fmaxf(le, E);
-      }
-      le = warp_max(le);
-      named_bar_sync(1, 128);
-      if (lane == 0) red[4 + ew] = le;
-      named_bar_sync(1, 128);
-      const float emax = fmaxf(fmaxf(red[4], red[5]), fmaxf(red[6], red[7]));
+      // ---- finalize: threshold, forcing, lists ----------------------------
+      named_bar_sync(1, 128);                      // stats, M and K complete
+      const float Mx = ord2f(sred[0]);
+      const float Kx = ord2f(sred[1]);
+      const float emax = (Mx == -INFINITY || Kx == -INFINITY) ? 0.f : ex2(Kx - Mx);
       const float thr = g.alpha * emax;
       const bool dense_tail = it.t >= max(g.Nt - g.last_n, 0);
       for (int base_b = ew * 32; base_b < Nb; base_b += 128) {
         const int b = base_b + lane;
         const long long bs = (long long)b * g.block_k, be = bs + g.block_k;
-        const float E = b < it.n_full ? stats[b].y : 0.f;
+        float E = 0.f;
+        if (b < it.n_full) {
+          const float2 st = stats[b];
+          E = (Mx == -INFINITY || st.x == -INFINITY) ? 0.f : st.y * ex2(st.x - Mx);
+        }
         const bool forced = bs < g.sink || be > it.tile_first - g.window || dense_tail;
         const bool fin = b < Nb && (E >= thr || forced) && bs <= it.tile_last;
         const bool pr = b < Nb && !fin && min(be, (long long)g.valid_lk) <= it.tile_first;
@@ -360,34 +412,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (p.mask != nullptr && b < Nb) p.mask[row_base + b] = (uint8_t)fin;
       }
-      named_bar_sync(1, 128);
-      if (p.sel_ids != nullptr) {
-        if (ew == 0) {
-          int run_s = 0, run_p = 0;
-          for (int w0 = 0; w0 < nwords; w0 += 32) {
-            const int wi = w0 + lane;
-            const int cs = wi < nwords ? __popc(selw[wi]) : 0;
-            const int cp = wi < nwords ? __popc(prw[wi]) : 0;
-            int is = cs, ip = cp;   // inclusive warp scan
+      named_bar_sync(1, 128);                      // words complete; M, K consumed
+      if (et == 0) {
+        sred[0] = f2ord(-INFINITY);
+        sred[1] = f2ord(-INFINITY);
+      }
+      if (p.sel_ids != nullptr && ew == 0) {
+        int run_s = 0, run_p = 0;
+        for (int w0 = 0; w0 < nwords; w0 += 32) {
+          const int wi = w0 + lane;
+          const int cs = wi < nwords ? __popc(selw[wi]) : 0;
+          const int cp = wi < nwords ? __popc(prw[wi]) : 0;
+          int is = cs, ip = cp;   // inclusive warp scan
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-              const int ys = __shfl_up_sync(0xffffffffu, is, o);
-              const int yp = __shfl_up_sync(0xffffffffu, ip, o);
-              if (lane >= o) { is += ys; ip += yp; }
-            }
-            if (wi < nwords) {
-              selpre[wi] = run_s + is - cs;
-              prpre[wi] = run_p + ip - cp;
-            }
-            run_s += __shfl_sync(0xffffffffu, is, 31);
-            run_p += __shfl_sync(0xffffffffu, ip, 31);
+          for (int o = 1; o < 32; o <<= 1) {
+            const int ys = __shfl_up_sync(0xffffffffu, is, o);
+            const int yp = __shfl_up_sync(0xffffffffu, ip, o);
+            if (lane >= o) { is += ys; ip += yp; }
           }
-          if (lane == 0) {
-            totals[0] = run_s;
-            totals[1] = run_p;
+          if (wi < nwords) {
+            selpre[wi] = run_s + is - cs;
+            prpre[wi] = run_p + ip - cp;
           }
+          run_s += __shfl_sync(0xffffffffu, is, 31);
+          run_p += __shfl_sync(0xffffffffu, ip, 31);
         }
-        named_bar_sync(1, 128);
+        if (lane == 0) {
+          totals[0] = run_s;
+          totals[1] = run_p;
+        }
+      }
+      named_bar_sync(1, 128);                      // prefixes complete
+      if (p.sel_ids != nullptr) {
         const int nsel = totals[0], npr = totals[1];
         for (int base_b = ew * 32; base_b < Nb; base_b += 128) {
           const int b = base_b + lane;
@@ -405,7 +461,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           p.pr_counts[(long long)it.h * g.Nt + it.t] = npr;
         }
       }
-      named_bar_sync(1, 128);
     }
   }
 
@@ -429,6 +484,7 @@ size_t smem_bytes(int Nb) {
 
 bool select_tc_supported(const SelectGeom& g, int dt) {
   if (dt != DT_BF16 && dt != DT_F16) return false;
+  if (!(g.scale > 0.f)) return false;
   if (g.D != 64 && g.D != 128) return false;
   if (g.Nb > kMaxNb || g.Nb <= 0) return false;
   const int R = g.G * g.tile_q;

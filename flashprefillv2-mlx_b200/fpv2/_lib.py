@@ -20,6 +20,7 @@ ERR_INVALID_ARGUMENT = 1
 ERR_UNSUPPORTED = 2
 ERR_CUDA = 3
 ERR_DEVICE_TIMEOUT = 4
+ATTN_WORKSPACE_BYTES = 16
 
 _DTYPE_CODES = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32}
 
@@ -64,7 +65,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
          ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
          ctypes.c_int, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
          ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_float,
-         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p],
+         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+         ctypes.c_int64, ctypes.c_void_p],
     ),
     "fpv2_fast_path_mask": (
         ctypes.c_int,

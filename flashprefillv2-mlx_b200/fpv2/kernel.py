@@ -215,13 +215,14 @@ def sparse_attention(
     pkc, pvc = pooled_k.contiguous(), pooled_v.contiguous()
     lc = [x.contiguous() for x in (selected_ids, selected_counts, pruned_ids, pruned_counts)]
     out = torch.empty_like(qc)
+    workspace = torch.empty(_lib.ATTN_WORKSPACE_BYTES // 4, dtype=torch.int32, device=q.device)
     _lib.check(_lib.lib().fpv2_sparse_attention(
         _lib.ptr(qc), _lib.ptr(kc), _lib.ptr(vc), _lib.ptr(pkc), _lib.ptr(pvc),
         _lib.dtype_code(pkc.dtype), _lib.ptr(lc[0]), _lib.ptr(lc[1]), _lib.ptr(lc[2]),
         _lib.ptr(lc[3]), _lib.dtype_code(q.dtype), query_heads, kv_heads, padded_query_length,
         padded_key_length, head_dim, offset, valid_query_length, valid_key_length, float(scale),
         config.block_k, config.tile_q, 1 if config.mean_correction else 0, _lib.ptr(out),
-        _lib.stream_of(q)))
+        _lib.ptr(workspace), workspace.numel() * 4, _lib.stream_of(q)))
     return out
 
 

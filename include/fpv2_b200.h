@@ -134,10 +134,16 @@ FPV2_API int fpv2_index_stage(const void* q, const void* k, const void* v, int d
  * shifted by log2(block_k). q/k/v/out share `dtype` (FPV2_F16 or FPV2_BF16);
  * pooled_k/pooled_v are `pooled_dtype` (dtype or FPV2_F32) and are rounded
  * to `dtype` on load. Ids are clipped to [0, num_blocks-1] and counts to
- * [0, num_blocks]. Rows >= query_length are padding; their output is unspecified.
+ * [0, num_blocks]; the pruned ids of a tile are treated as a set.
+ * Rows >= query_length are padding; their output is unspecified.
+ * `workspace` (nullable) is caller-owned device scratch of at least
+ * FPV2_ATTN_WORKSPACE_BYTES: the kernel's work-queue counter, rewritten on
+ * `stream` by every call (calls sharing one workspace must be stream-ordered).
+ * Without it the work is distributed statically (same results, slower).
  * Replaces fpv2/kernel.py:441-590 (sparse_attention) and its Metal kernel
  * fpv2/kernel.py:187-414.
  */
+#define FPV2_ATTN_WORKSPACE_BYTES 16
 FPV2_API int fpv2_sparse_attention(const void* q, const void* k, const void* v, const void* pooled_k,
                           const void* pooled_v, int pooled_dtype,
                           const int32_t* selected_ids, const int32_t* selected_counts,
@@ -146,7 +152,8 @@ FPV2_API int fpv2_sparse_attention(const void* q, const void* k, const void* v, 
                           int32_t padded_k_len, int32_t head_dim, int32_t offset,
                           int32_t query_length, int32_t key_length, float scale,
                           int32_t block_k, int32_t tile_q, int32_t mean_correction,
-                          void* out, void* stream);
+                          void* out, void* workspace, int64_t workspace_bytes,
+                          void* stream);
 
 /*
  * Which kernel family the two stages would use for this shape:

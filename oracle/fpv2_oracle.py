@@ -359,7 +359,8 @@ def sparse_attention(
     Per query row ``o = (sum_sel 2^(s2-m) v + sum_pruned 2^(s2p + log2 bk - m) vbar) / l``
     with ``s2 = scale*log2(e)*q.k``, masked logits at ``finite_min``, pooled K/V
     rounded to ``dtype`` (kernel.py:553-554) and lists clipped (kernel.py:555-558).
-    Inputs are float32 arrays carrying ``dtype`` values.  Rows at or beyond
+    Inputs are float32 arrays carrying ``dtype`` values; the output is rounded
+    to ``dtype`` as the kernel stores it (kernel.py:409).  Rows at or beyond
     ``query_length`` are padding and are returned as zeros.  ``tiles``
     restricts the evaluation to the listed (kv_head, tile) pairs.
     """
@@ -412,7 +413,7 @@ def sparse_attention(
         p = np.exp2(s - m)
         o = np.matmul(p, vals) / p.sum(axis=-1, keepdims=True)
         out[h * g:(h + 1) * g, rows, :] = o
-    return out
+    return round_to(out, dtype)
 
 
 def exact_causal_attention(q, k, v, scale: float, offset: int = 0) -> np.ndarray:
