@@ -335,6 +335,11 @@ def main(argv=None) -> int:
         import torch.distributed as dist
 
         dist.barrier()
+    from fpv2 import _lib as fpv2_lib
+
+    status = fpv2_lib.device_status(dev)
+    if status:
+        raise SystemExit(f"a kernel reported a bounded-wait timeout (status {status})")
     total_ms = start.elapsed_time(end)
     idx_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
     attn_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)

@@ -556,17 +556,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t vmask[4];
         if (rec.kind == KIND_SEL) {
           const long long ks = rec.kstart;
-          full = row_valid && ks + 127 <= position && ks + 127 < a.valid_lk;
+          const bool row_full = row_valid && ks + 127 <= position && ks + 127 < a.valid_lk;
+          // warp-uniform: a mixed warp takes the masked path on every lane
+          full = __all_sync(0xffffffffu, row_full);
           if (!full) {
+            // valid keys of this row: key <= position and key < valid_lk
+            const long long lim = row_valid ? min(position + 1, (long long)a.valid_lk) - ks : 0;
 #pragma unroll
             for (int q4 = 0; q4 < 4; ++q4) {
-              uint32_t m = 0u;
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const long long key = ks + q4 * 32 + j;
-                m |= (row_valid && key <= position && key < a.valid_lk) ? (1u << j) : 0u;
-              }
-              vmask[q4] = m;
+              const long long nv = lim - q4 * 32;
+              vmask[q4] = nv >= 32 ? 0xffffffffu : (nv <= 0 ? 0u : ((1u << nv) - 1u));
             }
           }
         } else if (rec.kind == KIND_POOL) {
@@ -598,10 +597,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            if ((vmask[0] >> j) & 1u) mx0 = fmaxf(mx0, __uint_as_float(s[0][j]));
-            if ((vmask[1] >> j) & 1u) mx1 = fmaxf(mx1, __uint_as_float(s[1][j]));
-            if ((vmask[2] >> j) & 1u) mx2 = fmaxf(mx2, __uint_as_float(s[2][j]));
-            if ((vmask[3] >> j) & 1u) mx3 = fmaxf(mx3, __uint_as_float(s[3][j]));
+            mx0 = ((vmask[0] >> j) & 1u) ? fmaxf(mx0, __uint_as_float(s[0][j])) : mx0;
+            mx1 = ((vmask[1] >> j) & 1u) ? fmaxf(mx1, __uint_as_float(s[1][j])) : mx1;
+            mx2 = ((vmask[2] >> j) & 1u) ? fmaxf(mx2, __uint_as_float(s[2][j])) : mx2;
+            mx3 = ((vmask[3] >> j) & 1u) ? fmaxf(mx3, __uint_as_float(s[3][j])) : mx3;
           }
         }
         const float mraw = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
@@ -648,8 +647,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             float p0 = ex2(fmaf(__uint_as_float(s[q4][j]), c2, neg_m));
             float p1 = ex2(fmaf(__uint_as_float(s[q4][j + 1]), c2, neg_m));
             if (!full) {
-              if (!((vmask[q4] >> j) & 1u)) p0 = masked_p;
-              if (!((vmask[q4] >> (j + 1)) & 1u)) p1 = masked_p;
+              p0 = ((vmask[q4] >> j) & 1u) ? p0 : masked_p;
+              p1 = ((vmask[q4] >> (j + 1)) & 1u) ? p1 : masked_p;
             }
             if (q4 == 0) rs0 += p0 + p1;
             else if (q4 == 1) rs1 += p0 + p1;

@@ -483,6 +483,7 @@ int fpv2_fast_path_mask(int dtype, int32_t q_heads, int32_t kv_heads, int32_t he
   g.Nb = num_blocks;
   g.block_k = block_k;
   g.tile_q = tile_q;
+  g.scale = 1.f;   // any positive softmax scale
   AttnArgs a{};
   a.dt = dtype;
   a.pooled_dt = dtype;

@@ -321,42 +321,54 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_wait_ld();
 #pragma unroll
             for (int q4 = 0; q4 < 4; ++q4) reg_fence(sv[q4]);
-            const uint32_t kNegInf = 0xff800000u;
-            if (!bvalid || it.row_mask) {
+            // Element masks are needed only for partially visible rows or a
+            // narrow N-chunk; the decision is per item, so it never diverges
+            // inside a warp. Lanes past the fully visible blocks compute on
+            // whatever the tile holds and are simply not recorded.
+            const bool masked = it.row_mask || p.NC < 128;
+            uint32_t vm[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+            if (masked) {
               const long long bstart = (long long)b * g.block_k;
-#pragma unroll
-              for (int q4 = 0; q4 < 4; ++q4)
-#pragma unroll
+#pragma unroll 1
+              for (int q4 = 0; q4 < 4; ++q4) {
+                uint32_t bits = 0u;
                 for (int j = 0; j < 32; ++j) {
                   const int col = q4 * 32 + j;
-                  bool v = bvalid && col < p.NC;
+                  bool v = col < p.NC;
                   if (v && it.row_mask) {
                     const int P = cc * p.NC + col;
                     const long long row = (long long)it.t * g.tile_q + P % g.tile_q;
                     v = row < g.valid_lq && bstart <= g.offset + row;
                   }
-                  if (!v) sv[q4][j] = kNegInf;
+                  bits |= v ? (1u << j) : 0u;
                 }
-            } else if (p.NC < 128) {
-#pragma unroll
-              for (int q4 = 0; q4 < 4; ++q4)
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (q4 * 32 + j >= p.NC) sv[q4][j] = kNegInf;
+                vm[q4] = bits;
+              }
             }
             float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+            if (!masked) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              m0 = fmaxf(m0, __uint_as_float(sv[0][j]));
-              m1 = fmaxf(m1, __uint_as_float(sv[1][j]));
-              m2 = fmaxf(m2, __uint_as_float(sv[2][j]));
-              m3 = fmaxf(m3, __uint_as_float(sv[3][j]));
+              for (int j = 0; j < 32; ++j) {
+                m0 = fmaxf(m0, __uint_as_float(sv[0][j]));
+                m1 = fmaxf(m1, __uint_as_float(sv[1][j]));
+                m2 = fmaxf(m2, __uint_as_float(sv[2][j]));
+                m3 = fmaxf(m3, __uint_as_float(sv[3][j]));
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                m0 = ((vm[0] >> j) & 1u) ? fmaxf(m0, __uint_as_float(sv[0][j])) : m0;
+                m1 = ((vm[1] >> j) & 1u) ? fmaxf(m1, __uint_as_float(sv[1][j])) : m1;
+                m2 = ((vm[2] >> j) & 1u) ? fmaxf(m2, __uint_as_float(sv[2][j])) : m2;
+                m3 = ((vm[3] >> j) & 1u) ? fmaxf(m3, __uint_as_float(sv[3][j])) : m3;
+              }
             }
             const float mraw = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
             const float mnew = fmaxf(mb, mraw * c);
-            if (mnew != -INFINITY) {
-              const float nm = -mnew;
-              float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
+            // all lanes take the same path below (-inf maxima give ex2(-inf) = 0)
+            const float nm = mnew == -INFINITY ? 0.f : -mnew;
+            float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
+            if (!masked) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
                 e0 += ex2(fmaf(__uint_as_float(sv[0][j]), c, nm));
@@ -364,6 +376,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 e2 += ex2(fmaf(__uint_as_float(sv[2][j]), c, nm));
                 e3 += ex2(fmaf(__uint_as_float(sv[3][j]), c, nm));
               }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float x0 = ex2(fmaf(__uint_as_float(sv[0][j]), c, nm));
+                const float x1 = ex2(fmaf(__uint_as_float(sv[1][j]), c, nm));
+                const float x2 = ex2(fmaf(__uint_as_float(sv[2][j]), c, nm));
+                const float x3 = ex2(fmaf(__uint_as_float(sv[3][j]), c, nm));
+                e0 += ((vm[0] >> j) & 1u) ? x0 : 0.f;
+                e1 += ((vm[1] >> j) & 1u) ? x1 : 0.f;
+                e2 += ((vm[2] >> j) & 1u) ? x2 : 0.f;
+                e3 += ((vm[3] >> j) & 1u) ? x3 : 0.f;
+              }
+            }
+            if (mnew != -INFINITY) {
               eb = eb * ex2(mb - mnew) + ((e0 + e1) + (e2 + e3));
               mb = mnew;
             }

@@ -152,6 +152,23 @@ def fpv2_sdpa(
     return output[None, :, :query_length, :]
 
 
+def _call_original(*args: Any, **kwargs: Any) -> torch.Tensor:
+    """Call torch's own SDPA exactly as the caller asked.
+
+    A ``CausalBias`` mask dispatches through ``__torch_function__``, which only
+    recognises the call while the module attribute is torch's function, so the
+    original is put back for the duration of such a call.
+    """
+    if CausalBias is not None and isinstance(kwargs.get("attn_mask"), CausalBias):
+        current = F.scaled_dot_product_attention
+        F.scaled_dot_product_attention = _ORIGINAL_SDPA
+        try:
+            return _ORIGINAL_SDPA(*args, **kwargs)
+        finally:
+            F.scaled_dot_product_attention = current
+    return _ORIGINAL_SDPA(*args, **kwargs)
+
+
 def _causal_offset(q: torch.Tensor, k: torch.Tensor, attn_mask: object, is_causal: bool) -> int | None:
     """Offset of a bottom-right causal call, or None when the call is not one."""
     if q.ndim != 4 or k.ndim != 4:
@@ -265,7 +282,7 @@ def enable(
             )
             _selected_dense_blocks += visible
             _visible_blocks += visible
-        return _ORIGINAL_SDPA(
+        return _call_original(
             query, key, value, attn_mask=attn_mask, dropout_p=dropout_p, is_causal=is_causal,
             scale=scale, enable_gqa=enable_gqa, **kwargs
         )

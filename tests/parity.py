@@ -88,6 +88,13 @@ def kernel_errors(actual: torch.Tensor, expected: np.ndarray):
     return float((err / np.maximum(1.0, np.abs(expected))).max()), float(err.mean())
 
 
+def reference_rel_max(actual: torch.Tensor, expected: np.ndarray) -> float:
+    """max |a - b| / max |b|: the criterion of the reference's own kernel tests
+    (tests/test_kernel.py:221-224 of the reference)."""
+    a = np32(actual)
+    return float(np.abs(a - expected).max() / max(float(np.abs(expected).max()), 1e-8))
+
+
 def attention_errors(actual: torch.Tensor, expected: np.ndarray, rows: int | None = None):
     a = np32(actual)
     if rows is not None:

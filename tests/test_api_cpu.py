@@ -155,3 +155,23 @@ def test_enable_disable_restores_original():
     assert torch.equal(out, _ORIGINAL_SDPA(q, q, q, is_causal=True))
     fpv2.disable()
     assert not fpv2.is_enabled() and F.scaled_dot_product_attention is _ORIGINAL_SDPA
+
+
+def test_causal_bias_fall_through_is_bit_identical_on_cpu():
+    """A lower-right CausalBias call the hook does not claim reaches torch unchanged."""
+    import torch.nn.functional as F
+    from torch.nn.attention.bias import causal_lower_right
+
+    from fpv2.patch import _ORIGINAL_SDPA
+
+    q = torch.randn(1, 4, 8, 16)
+    k = torch.randn(1, 4, 24, 16)
+    v = torch.randn(1, 4, 24, 16)
+    bias = causal_lower_right(8, 24)
+    expected = _ORIGINAL_SDPA(q, k, v, attn_mask=bias)
+    fpv2.enable(min_tokens=1)
+    try:
+        actual = F.scaled_dot_product_attention(q, k, v, attn_mask=bias)
+    finally:
+        fpv2.disable()
+    assert torch.equal(actual, expected)
