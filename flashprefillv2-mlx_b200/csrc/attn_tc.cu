@@ -23,12 +23,14 @@
 // the reference kernel. Tiles without a pruned entry are skipped. (Pooled
 // inputs in float32 are rounded on a gathered path instead.)
 //
-// Warp roles (192 threads, one persistent CTA per SM):
+// Warp roles (320 threads, one persistent CTA per SM):
 //   warp 0     producer: takes work items from a global counter (largest
 //              first), walks the lists, publishes one record per KV item and
 //              loads Q / K / V / pooled tiles with TMA (no multicast);
 //   warp 1     MMA issuer;
-//   warps 2-5  softmax (thread = query row) and the output epilogue.
+//   warps 2-9  softmax and the output epilogue: two warps per TMEM lane
+//              quarter (thread = query row), each owning 64 of the 128 keys
+//              of an S tile and half of O's columns.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -36,7 +38,7 @@ namespace fpv2 {
 
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;   // producer, MMA, 8 softmax warps
 constexpr int kStages = 2;      // K/V tiles and S buffers
 constexpr int kRecs = 8;        // item records in flight
 constexpr int kTmemCols = 512;
@@ -118,7 +120,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* after_tiles = gbase + (2 + 2 * kStages) * C::kTileBytes;
   Rec* recs = reinterpret_cast<Rec*>(after_tiles);                // [kRecs]
   uint32_t* pmask = reinterpret_cast<uint32_t*>(recs + kRecs);    // producer-private [64]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(pmask + kMaskWordsMax);
+  float* pmax = reinterpret_cast<float*>(pmask + kMaskWordsMax);  // [2 parity][2 half][128]
+  float* lsum = pmax + 2 * 2 * 128;                                // [2 parity][2 half][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(lsum + 2 * 2 * 128);
   uint64_t* q_full = bars;              // [2]
   uint64_t* q_empty = q_full + 2;       // [2]
   uint64_t* rec_full = q_empty + 2;     // [kRecs]
@@ -134,7 +138,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* o_full = pv_done + 1;        // [1]
   uint64_t* o_free = o_full + 1;         // [1]
   uint64_t* drain = o_free + 1;          // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* xbar = drain + 1;            // [4] row-max exchange of a warp pair
+  uint64_t* lbar = xbar + 4;             // [4] row-sum exchange of a warp pair
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(lbar + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -147,7 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < kRecs; ++i) {
       mbar_init(smem_u32(&rec_full[i]), 1);
-      mbar_init(smem_u32(&rec_empty[i]), 1 + 4);   // MMA thread + 4 softmax warps
+      mbar_init(smem_u32(&rec_empty[i]), 1 + 8);   // MMA thread + 8 softmax warps
     }
     for (int i = 0; i < kStages; ++i) {
       mbar_init(smem_u32(&k_full[i]), 1);
@@ -156,12 +162,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&v_empty[i]), 1);
       mbar_init(smem_u32(&s_full[i]), 1);
       mbar_init(smem_u32(&s_free[i]), 1);
-      mbar_init(smem_u32(&p_full[i]), 4);
+      mbar_init(smem_u32(&p_full[i]), 8);
     }
     mbar_init(smem_u32(pv_done), 1);
     mbar_init(smem_u32(o_full), 1);
-    mbar_init(smem_u32(o_free), 4);
+    mbar_init(smem_u32(o_free), 8);
     mbar_init(smem_u32(drain), 1);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(smem_u32(&xbar[i]), 2);
+      mbar_init(smem_u32(&lbar[i]), 2);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -502,18 +512,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ======================= softmax + epilogue ============================
+    // Eight warps: warp w serves TMEM lane quarter w % 4 (query rows
+    // 32*(w%4) .. +31) and column half (w - 2) / 4 of every S tile (64 keys).
+    // The two warps of a quarter combine their row maxima through shared
+    // memory (a 2-arrival mbarrier per quarter), keep separate partial row sums, and rescale /
+    // store their own half of O's columns.
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;           // 0: columns [0, 64), 1: [64, 128)
     const int r = quarter * 32 + lane;          // row of the 128-row chunk
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const float c2 = a.scale_log2;
     int icount = 0, kv = 0, wi = 0;
     bool ok = true;
-    // Per work item state.
     Chunk ck{};
     int gq = 0;
     long long row = 0, position = 0;
     bool row_valid = false;
-    float m_used = kFiniteMin, l = 0.f;
+    float m_used = kFiniteMin, l = 0.f;   // l: this warp's half of the row sum
     int pv_wi = 0;
     while (ok) {
       const int ri = icount % kRecs;
@@ -544,66 +559,68 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         tc_fence_after();
         const uint32_t s_tmem = tmem_base + lane_off + C::kSCol + st * 128;
-        uint32_t s[4][32];
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(s_tmem + q4 * 32, s[q4]);
+        uint32_t s[2][32];
+        tmem_ld32(s_tmem + half * 64, s[0]);
+        tmem_ld32(s_tmem + half * 64 + 32, s[1]);
         tmem_wait_ld();
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) reg_fence(s[q4]);
-        // x = logit (base 2) of each key/entry; masked -> finite_min.
+        reg_fence(s[0]);
+        reg_fence(s[1]);
+        // validity of this warp's 64 entries; a mixed warp masks on every lane
         float bias = 0.f;
-        bool full;
-        uint32_t vmask[4];
+        uint32_t vm0 = 0xffffffffu, vm1 = 0xffffffffu;
+        bool full = true;
         if (rec.kind == KIND_SEL) {
-          const long long ks = rec.kstart;
-          const bool row_full = row_valid && ks + 127 <= position && ks + 127 < a.valid_lk;
-          // warp-uniform: a mixed warp takes the masked path on every lane
+          const long long ks = rec.kstart + half * 64;
+          const bool row_full = row_valid && ks + 63 <= position && ks + 63 < a.valid_lk;
           full = __all_sync(0xffffffffu, row_full);
           if (!full) {
-            // valid keys of this row: key <= position and key < valid_lk
             const long long lim = row_valid ? min(position + 1, (long long)a.valid_lk) - ks : 0;
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-              const long long nv = lim - q4 * 32;
-              vmask[q4] = nv >= 32 ? 0xffffffffu : (nv <= 0 ? 0u : ((1u << nv) - 1u));
-            }
+            vm0 = lim >= 32 ? 0xffffffffu : (lim <= 0 ? 0u : ((1u << lim) - 1u));
+            const long long lim1 = lim - 32;
+            vm1 = lim1 >= 32 ? 0xffffffffu : (lim1 <= 0 ? 0u : ((1u << lim1) - 1u));
           }
         } else if (rec.kind == KIND_POOL) {
           bias = a.corr_shift;
           full = false;
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) vmask[q4] = rec.mask[q4];
+          vm0 = rec.mask[2 * half];
+          vm1 = rec.mask[2 * half + 1];
         } else {   // KIND_CORR
           bias = a.corr_shift;
-          full = rec.nvalid >= 128;
+          const int nv = rec.nvalid - half * 64;
+          full = nv >= 64;
           if (!full) {
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-              const int nv = rec.nvalid - q4 * 32;
-              vmask[q4] = nv >= 32 ? 0xffffffffu : (nv <= 0 ? 0u : ((1u << nv) - 1u));
-            }
+            vm0 = nv >= 32 ? 0xffffffffu : (nv <= 0 ? 0u : ((1u << nv) - 1u));
+            const int nv1 = nv - 32;
+            vm1 = nv1 >= 32 ? 0xffffffffu : (nv1 <= 0 ? 0u : ((1u << nv1) - 1u));
           }
         }
-        // Row max over valid entries (raw scores; c2 > 0 so the order is kept).
+        // partial row max over valid raw scores (c2 > 0 keeps the order)
         float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
         if (full) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
+          for (int j = 0; j < 32; j += 2) {
             mx0 = fmaxf(mx0, __uint_as_float(s[0][j]));
-            mx1 = fmaxf(mx1, __uint_as_float(s[1][j]));
-            mx2 = fmaxf(mx2, __uint_as_float(s[2][j]));
-            mx3 = fmaxf(mx3, __uint_as_float(s[3][j]));
+            mx1 = fmaxf(mx1, __uint_as_float(s[0][j + 1]));
+            mx2 = fmaxf(mx2, __uint_as_float(s[1][j]));
+            mx3 = fmaxf(mx3, __uint_as_float(s[1][j + 1]));
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            mx0 = ((vmask[0] >> j) & 1u) ? fmaxf(mx0, __uint_as_float(s[0][j])) : mx0;
-            mx1 = ((vmask[1] >> j) & 1u) ? fmaxf(mx1, __uint_as_float(s[1][j])) : mx1;
-            mx2 = ((vmask[2] >> j) & 1u) ? fmaxf(mx2, __uint_as_float(s[2][j])) : mx2;
-            mx3 = ((vmask[3] >> j) & 1u) ? fmaxf(mx3, __uint_as_float(s[3][j])) : mx3;
+          for (int j = 0; j < 32; j += 2) {
+            mx0 = ((vm0 >> j) & 1u) ? fmaxf(mx0, __uint_as_float(s[0][j])) : mx0;
+            mx1 = ((vm0 >> (j + 1)) & 1u) ? fmaxf(mx1, __uint_as_float(s[0][j + 1])) : mx1;
+            mx2 = ((vm1 >> j) & 1u) ? fmaxf(mx2, __uint_as_float(s[1][j])) : mx2;
+            mx3 = ((vm1 >> (j + 1)) & 1u) ? fmaxf(mx3, __uint_as_float(s[1][j + 1])) : mx3;
           }
         }
-        const float mraw = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        const float mraw_half = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        pmax[((kv & 1) * 2 + half) * 128 + r] = mraw_half;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&xbar[quarter]));
+        ok = mbar_wait(smem_u32(&xbar[quarter]), kv & 1, wc);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        const float mraw = fmaxf(mraw_half, pmax[((kv & 1) * 2 + (half ^ 1)) * 128 + r]);
         const float mt = mraw == -INFINITY ? kFiniteMin : fmaf(mraw, c2, bias);
         const float m_new = fmaxf(m_used, mt);
         const bool need = m_new > m_used + kRescaleThreshold ||
@@ -615,15 +632,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             l *= f;
           }
           if (pv_wi > 0) {
-            // O holds PVs of this work item: wait for the latest one, rescale rows.
+            // O holds PVs of this work item: wait for the latest one, rescale this
+            // warp's half of the row's columns.
             ok = mbar_wait(smem_u32(pv_done), (kv - 1) & 1, wc);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc_fence_after();
 #pragma unroll
-            for (int dc = 0; dc < D / 32; ++dc) {
+            for (int dc = 0; dc < D / 64; ++dc) {
               uint32_t o[32];
-              const uint32_t oaddr = tmem_base + lane_off + C::kOCol + dc * 32;
+              const uint32_t oaddr = tmem_base + lane_off + C::kOCol + half * (D / 2) + dc * 32;
               tmem_ld32(oaddr, o);
               tmem_wait_ld();
               reg_fence(o);
@@ -639,27 +657,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float neg_m = bias - m_used;
         const float masked_p = (m_used == kFiniteMin) ? 1.f : 0.f;
         float rs0 = 0.f, rs1 = 0.f, rs2 = 0.f, rs3 = 0.f;
-        uint32_t pk[2][32];
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t pk[32];
+        if (full) {
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            float p0 = ex2(fmaf(__uint_as_float(s[q4][j]), c2, neg_m));
-            float p1 = ex2(fmaf(__uint_as_float(s[q4][j + 1]), c2, neg_m));
-            if (!full) {
-              p0 = ((vmask[q4] >> j) & 1u) ? p0 : masked_p;
-              p1 = ((vmask[q4] >> (j + 1)) & 1u) ? p1 : masked_p;
-            }
-            if (q4 == 0) rs0 += p0 + p1;
-            else if (q4 == 1) rs1 += p0 + p1;
-            else if (q4 == 2) rs2 += p0 + p1;
-            else rs3 += p0 + p1;
-            pk[q4 >> 1][(q4 & 1) * 16 + (j >> 1)] = pack2<DT>(p0, p1);
+            const float p0 = ex2(fmaf(__uint_as_float(s[0][j]), c2, neg_m));
+            const float p1 = ex2(fmaf(__uint_as_float(s[0][j + 1]), c2, neg_m));
+            const float p2 = ex2(fmaf(__uint_as_float(s[1][j]), c2, neg_m));
+            const float p3 = ex2(fmaf(__uint_as_float(s[1][j + 1]), c2, neg_m));
+            rs0 += p0;
+            rs1 += p1;
+            rs2 += p2;
+            rs3 += p3;
+            pk[j >> 1] = pack2<DT>(p0, p1);
+            pk[16 + (j >> 1)] = pack2<DT>(p2, p3);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            float p0 = ex2(fmaf(__uint_as_float(s[0][j]), c2, neg_m));
+            float p1 = ex2(fmaf(__uint_as_float(s[0][j + 1]), c2, neg_m));
+            float p2 = ex2(fmaf(__uint_as_float(s[1][j]), c2, neg_m));
+            float p3 = ex2(fmaf(__uint_as_float(s[1][j + 1]), c2, neg_m));
+            p0 = ((vm0 >> j) & 1u) ? p0 : masked_p;
+            p1 = ((vm0 >> (j + 1)) & 1u) ? p1 : masked_p;
+            p2 = ((vm1 >> j) & 1u) ? p2 : masked_p;
+            p3 = ((vm1 >> (j + 1)) & 1u) ? p3 : masked_p;
+            rs0 += p0;
+            rs1 += p1;
+            rs2 += p2;
+            rs3 += p3;
+            pk[j >> 1] = pack2<DT>(p0, p1);
+            pk[16 + (j >> 1)] = pack2<DT>(p2, p3);
           }
         }
         l += (rs0 + rs1) + (rs2 + rs3);
-        tmem_st32(s_tmem, pk[0]);
-        tmem_st32(s_tmem + 32, pk[1]);
+        // P of keys [64 half, +64) -> TMEM columns [32 half, +32) of the S buffer
+        tmem_st32(s_tmem + half * 32, pk);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -669,19 +703,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (rec.flags & 2) {
         // ---- epilogue: O / l -> out ----------------------------------------
+        lsum[((wi & 1) * 2 + half) * 128 + r] = l;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&lbar[quarter]));
+        ok = mbar_wait(smem_u32(&lbar[quarter]), wi & 1, wc);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        const float lrow = l + lsum[((wi & 1) * 2 + (half ^ 1)) * 128 + r];
         ok = mbar_wait(smem_u32(o_full), wi & 1, wc);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
         using T = typename Elem<DT>::T;
         T* out = reinterpret_cast<T*>(a.out) +
-                 (((long long)(ck.h * a.G + gq)) * a.Lq_pad + row) * D;
-        const float inv = pv_wi > 0 ? 1.f / l : 0.f;
+                 (((long long)(ck.h * a.G + gq)) * a.Lq_pad + row) * D + half * (D / 2);
+        const float inv = pv_wi > 0 ? 1.f / lrow : 0.f;
 #pragma unroll
-        for (int dc = 0; dc < D / 32; ++dc) {
+        for (int dc = 0; dc < D / 64; ++dc) {
           uint32_t o[32];
           if (pv_wi > 0) {
-            tmem_ld32(tmem_base + lane_off + C::kOCol + dc * 32, o);
+            tmem_ld32(tmem_base + lane_off + C::kOCol + half * (D / 2) + dc * 32, o);
             tmem_wait_ld();
             reg_fence(o);
           } else {
@@ -714,7 +755,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int D>
 size_t smem_bytes() {
   return 1024 + (size_t)(2 + 2 * kStages) * Cfg<D>::kTileBytes + sizeof(Rec) * kRecs +
-         4 * kMaskWordsMax + 8 * (4 + 2 * kRecs + 7 * kStages + 4) + 16;
+         4 * kMaskWordsMax + 4 * (4 * 128 + 4 * 128) + 8 * (4 + 2 * kRecs + 7 * kStages + 12) + 16;
 }
 
 }  // namespace
