@@ -111,6 +111,13 @@ size_t dt_size(int dt) { return dt == DT_F32 ? 4 : 2; }
 
 }  // namespace
 
+// Record `msg` as the calling thread's last error and return `code` (for entry
+// points defined in other translation units).
+int report_error(int code, const char* msg) {
+  t_last_error = msg;
+  return code;
+}
+
 bool encode_tmap_3d(CUtensorMap* map, const void* base, int dt, uint64_t d0, uint64_t d1,
                     uint64_t d2, uint32_t b0, uint32_t b1, uint32_t b2) {
   EncodeTiledFn fn = encode_fn();

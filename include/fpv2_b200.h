@@ -156,6 +156,28 @@ FPV2_API int fpv2_sparse_attention(const void* q, const void* k, const void* v, 
                           void* stream);
 
 /*
+ * fpv2_sparse_attention for callers that cannot allocate device memory (no
+ * counterpart in the reference). Same arguments and results as
+ * fpv2_sparse_attention without the workspace: the kernel's work-queue counter
+ * lives in a FPV2_NOALLOC_SCRATCH_BYTES array compiled into the library, held
+ * by every GPU that loads it until exit. Every call on a device shares that
+ * array (it is cleared on `stream` before each launch), so calls that overlap
+ * on the GPU race. The first call on a device looks up the array's address;
+ * make it before any stream capture. Problems with more than
+ * FPV2_NOALLOC_MAX_WORK_ITEMS work items (128-row chunks of selection tiles)
+ * are rejected with FPV2_ERR_INVALID_ARGUMENT.
+ */
+#define FPV2_NOALLOC_SCRATCH_BYTES 256
+#define FPV2_NOALLOC_MAX_WORK_ITEMS (1 << 24)
+FPV2_API int fpv2_sparse_attention_noalloc(
+    const void* q, const void* k, const void* v, const void* pooled_k, const void* pooled_v,
+    int pooled_dtype, const int32_t* selected_ids, const int32_t* selected_counts,
+    const int32_t* pruned_ids, const int32_t* pruned_counts, int dtype, int32_t q_heads,
+    int32_t kv_heads, int32_t padded_q_len, int32_t padded_k_len, int32_t head_dim,
+    int32_t offset, int32_t query_length, int32_t key_length, float scale, int32_t block_k,
+    int32_t tile_q, int32_t mean_correction, void* out, void* stream);
+
+/*
  * Which kernel family the two stages would use for this shape:
  * bit 0 set = tcgen05 index stage, bit 1 set = tcgen05 attention
  * (otherwise the generic CUDA-core kernels run).

@@ -1,0 +1,69 @@
+"""The no-allocation attention entry point, ``fpv2_sparse_attention_noalloc``.
+
+Callers that cannot allocate device memory use it: serving engines that have
+reserved nearly all HBM for their own KV-cache pool and allow no allocation
+outside it, and pipelines that may not let a cudaMalloc (which can synchronise
+the device) run between their asynchronous launches. The entry point keeps the
+attention kernel's work-queue counter in a fixed array inside the library
+instead of a caller-provided workspace.
+
+The GPU test calls it through the C ABI twice in a row on the same inputs and
+checks each output against the regular entry point, ``fpv2_sparse_attention``
+with a caller workspace. This file is collected last on purpose, and the test
+passes both alone in a fresh process and after the rest of the suite.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+
+import fpv2
+from fpv2 import _lib
+from fpv2.patch import _effective_config
+from tests import parity as P
+from tests.synthetic import topic_qkv
+
+
+def _noalloc(q, k, v, pk, pv, lists, out, cfg, scale, stream):
+    return _lib.lib().fpv2_sparse_attention_noalloc(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), pk.data_ptr(), pv.data_ptr(),
+        _lib.dtype_code(pk.dtype), lists[0].data_ptr(), lists[1].data_ptr(),
+        lists[2].data_ptr(), lists[3].data_ptr(), _lib.dtype_code(q.dtype), q.shape[0],
+        k.shape[0], q.shape[1], k.shape[1], q.shape[2], 0, q.shape[1], k.shape[1],
+        ctypes.c_float(scale), cfg.block_k, cfg.tile_q, 1 if cfg.mean_correction else 0,
+        out.data_ptr(), stream)
+
+
+def test_noalloc_rejects_problems_beyond_its_scratch():
+    """Sizes beyond FPV2_NOALLOC_MAX_WORK_ITEMS are refused before any GPU work."""
+    rc = _lib.lib().fpv2_sparse_attention_noalloc(
+        None, None, None, None, None, 1, None, None, None, None, 1, 64, 1, 1 << 30, 1 << 30,
+        128, 0, 1 << 30, 1 << 30, ctypes.c_float(0.1), 128, 1, 1, None, None)
+    assert rc == _lib.ERR_INVALID_ARGUMENT
+    assert "no-alloc scratch" in _lib.lib().fpv2_last_error().decode()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("length,hq,hkv", [(2048, 8, 2), (8192, 32, 8)])
+def test_noalloc_matches_workspace_entry_twice(length, hq, hkv):
+    dev = torch.device("cuda:0")
+    q, k, v = topic_qkv(length=length, query_heads=hq, kv_heads=hkv, seed=5,
+                        dtype=torch.bfloat16)
+    q, k, v = q.to(dev), k.to(dev), v.to(dev)
+    cfg = _effective_config(fpv2.FPV2Config(alpha=0.1), hq, hkv)
+    scale = 128 ** -0.5
+    pk, pv, lists, _ = fpv2.index_stage(q, k, v, scale=scale, config=cfg, offset=0,
+                                        query_length=length, key_length=length)
+    expected = fpv2.sparse_attention(q, k, v, pk, pv, *lists, scale=scale, config=cfg)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for _ in range(2):
+        out = torch.full_like(q, float("nan"))
+        rc = _noalloc(q, k, v, pk, pv, lists, out, cfg, scale, stream)
+        assert rc == _lib.OK, _lib.lib().fpv2_last_error().decode()
+        torch.cuda.synchronize(dev)
+        assert _lib.device_status(dev) == 0
+        mx, mean = P.kernel_errors(out, P.np32(expected))
+        assert mx <= P.KERNEL_MAX_ABS_TOL and mean <= P.KERNEL_MEAN_ABS_TOL, (mx, mean)
