@@ -13,14 +13,17 @@
 // are register-local. The tile max is then M = max_b m_b and
 // E[b] = e_b * 2^(m_b - M): no cross-thread reduction touches the N*Nb scores.
 //
-// Warp roles (192 threads, one persistent CTA per SM):
+// Warp roles (320 threads, one persistent CTA per SM):
 //   warp 0  TMA producer: Q chunks [N x D] and pooled-K tiles [128 x D], 128B swizzle.
 //           A pooled-K tile stays in its ring slot while the CTA keeps the same
 //           KV head, so pooled K is read from L2 once per CTA when Nb <= 128*slots.
 //   warp 1  MMA issuer (tcgen05.mma kind::f16, fp32 accumulators in TMEM).
-//   warps 2-5  energy + finalize: TMEM -> registers, masked max / exp2-sums,
-//           then threshold, forcing and ballot-based compaction into the
-//           full-width padded lists.
+//   warps 2-5, 6-9  two energy + finalize groups: TMEM -> registers, masked
+//           max / exp2-sums, then threshold, forcing and ballot-based
+//           compaction into the full-width padded lists. The groups take a
+//           CTA's items alternately (each owns two TMEM slots and its own
+//           statistics), so one group's finalize overlaps the other group's
+//           exponentials and each SM sub-partition has two warps issuing ex2.
 // Work items are (kv head, tile) with tiles latest-first; CTA c keeps KV head
 // c % Hkv whenever the grid is a multiple of Hkv.
 #include "common.cuh"
@@ -30,24 +33,27 @@ namespace fpv2 {
 
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kGroups = 2;           // energy/finalize warp groups
+constexpr int kThreads = 64 + kGroups * 128;
 constexpr int kTmemCols = 512;
 constexpr int kTmemSlots = 4;        // 128 columns each
+constexpr int kSlotsPerGroup = kTmemSlots / kGroups;
 constexpr int kMaxNb = 2048;
+constexpr int kSmemLimit = 227 * 1024;
 
 template <int D>
 struct Cfg {
   static constexpr int kHalves = D / 64;
   static constexpr int kQStages = 2;
-  static constexpr int kKStages = (D == 64) ? 8 : 4;
+  static constexpr int kKStagesMax = (D == 64) ? 8 : 4;   // pooled-K ring (runtime count)
   static constexpr int kQBytes = 128 * D * 2;   // up to 128 rows per chunk
   static constexpr int kKBytes = 128 * D * 2;
-  static constexpr int kOpBytes = kQStages * kQBytes + kKStages * kKBytes;
 };
 
 struct Params {
   SelectGeom g;
   int NC, box_rows, n_chunks;
+  int k_stages;                      // pooled-K ring slots in use (<= kKStagesMax)
   uint32_t idesc;
   float scale_log2;
   uint8_t* mask;
@@ -119,26 +125,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nwords = (Nb + 31) / 32;
 
   // ---- shared memory carve-up -------------------------------------------
+  const int KS = p.k_stages;
   const uint32_t q_smem = base;
   const uint32_t k_smem = base + C::kQStages * C::kQBytes;
-  float2* stats = reinterpret_cast<float2*>(gbase + C::kOpBytes);          // [Nb]
-  uint32_t* selw = reinterpret_cast<uint32_t*>(stats + Nb);               // [nwords]
-  uint32_t* prw = selw + nwords;
-  int* selpre = reinterpret_cast<int*>(prw + nwords);                     // [nwords]
-  int* prpre = selpre + nwords;
+  // per energy group: stats [Nb], selected / pruned words and their prefixes [nwords]
+  float2* stats_all = reinterpret_cast<float2*>(gbase + C::kQStages * C::kQBytes +
+                                                KS * C::kKBytes);      // [kGroups][Nb]
+  uint32_t* words_all = reinterpret_cast<uint32_t*>(stats_all + kGroups * Nb);  // [kGroups][4][nwords]
   uint64_t* bars = reinterpret_cast<uint64_t*>(
-      (reinterpret_cast<uintptr_t>(prpre + nwords) + 7) & ~uintptr_t(7));
+      (reinterpret_cast<uintptr_t>(words_all + kGroups * 4 * nwords) + 7) & ~uintptr_t(7));
   uint64_t* q_full = bars;
   uint64_t* q_empty = q_full + C::kQStages;
   uint64_t* k_full = q_empty + C::kQStages;
-  uint64_t* k_empty = k_full + C::kKStages;
-  uint64_t* t_full = k_empty + C::kKStages;
+  uint64_t* k_empty = k_full + C::kKStagesMax;
+  uint64_t* t_full = k_empty + C::kKStagesMax;
   uint64_t* t_empty = t_full + kTmemSlots;
   uint64_t* drain = t_empty + kTmemSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint32_t* sred = tmem_slot + 2;                          // [2] ordered-int M, K
-  int* totals = reinterpret_cast<int*>(sred + 2);          // [2]
+  uint32_t* sred_all = tmem_slot + 2;                      // [kGroups][2] ordered-int M, K
+  int* totals_all = reinterpret_cast<int*>(sred_all + 2 * kGroups);   // [kGroups][2]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -148,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&q_full[i]), 1);
       mbar_init(smem_u32(&q_empty[i]), 1);
     }
-    for (int i = 0; i < C::kKStages; ++i) {
+    for (int i = 0; i < C::kKStagesMax; ++i) {
       mbar_init(smem_u32(&k_full[i]), 1);
       mbar_init(smem_u32(&k_empty[i]), 1);
     }
@@ -179,10 +185,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ======================= TMA producer =================================
     if (lane == 0) {
       int qcount = 0;
-      int kuse[C::kKStages];
-      int ktag[C::kKStages];
+      int kuse[C::kKStagesMax];
+      int ktag[C::kKStagesMax];
 #pragma unroll
-      for (int i = 0; i < C::kKStages; ++i) { kuse[i] = 0; ktag[i] = -1; }
+      for (int i = 0; i < C::kKStagesMax; ++i) { kuse[i] = 0; ktag[i] = -1; }
       bool ok = true;
       for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x) {
         const Item it = make_item(p, w);
@@ -201,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_3d(q_smem + qs * C::kQBytes + hh * p.NC * 128, &tmap_q, qb, hh * 64,
                         it.t * g.tile_q + p0, it.h * g.G + g0);
           for (int m = 0; m < it.n_mt; ++m) {
-            const int s = m % C::kKStages;
+            const int s = m % KS;
             ok = mbar_wait(smem_u32(&k_empty[s]), (kuse[s] & 1) ^ 1, wc);
             if (!ok) break;
             ++kuse[s];
@@ -222,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Drain: wait (bounded) for every armed barrier phase so no bulk copy is
       // still writing shared memory when the CTA retires.
-      for (int i = 0; i < C::kKStages; ++i)
+      for (int i = 0; i < KS; ++i)
         if (kuse[i] > 0) mbar_wait(smem_u32(&k_full[i]), (kuse[i] - 1) & 1, wc, false);
       for (int i = 0; i < C::kQStages && i < qcount; ++i) {
         const int uses = (qcount - i + C::kQStages - 1) / C::kQStages;
@@ -232,28 +238,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ======================= MMA issuer ===================================
     if (lane == 0) {
-      int qcount = 0, tcount = 0;
-      int kuse[C::kKStages];
+      int qcount = 0;
+      int tcount[kGroups] = {0, 0};
+      int kuse[C::kKStagesMax];
 #pragma unroll
-      for (int i = 0; i < C::kKStages; ++i) kuse[i] = 0;
+      for (int i = 0; i < C::kKStagesMax; ++i) kuse[i] = 0;
       bool ok = true;
-      for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x) {
+      int j = 0;   // CTA-local item index: item j belongs to energy group j % kGroups
+      for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x, ++j) {
         const Item it = make_item(p, w);
         if (it.n_mt == 0) continue;
+        const int grp = j % kGroups;
         for (int c = 0; c < p.n_chunks && ok; ++c) {
           const int qs = qcount % C::kQStages;
           ok = mbar_wait(smem_u32(&q_full[qs]), (qcount / C::kQStages) & 1, wc);
           if (!ok) break;
           ++qcount;
           for (int m = 0; m < it.n_mt; ++m) {
-            const int s = m % C::kKStages;
+            const int s = m % KS;
             ok = mbar_wait(smem_u32(&k_full[s]), kuse[s] & 1, wc);
             if (!ok) break;
             ++kuse[s];
-            const int ts = tcount % kTmemSlots;
-            ok = mbar_wait(smem_u32(&t_empty[ts]), ((tcount / kTmemSlots) & 1) ^ 1, wc);
+            const int tc = tcount[grp];
+            const int ts = grp * kSlotsPerGroup + tc % kSlotsPerGroup;
+            ok = mbar_wait(smem_u32(&t_empty[ts]), ((tc / kSlotsPerGroup) & 1) ^ 1, wc);
             if (!ok) break;
-            ++tcount;
+            ++tcount[grp];
             tc_fence_after();
             const uint32_t d_tmem = tmem_base + ts * 128;
 #pragma unroll
@@ -282,25 +292,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     // e_b = sum_rows 2^(x - m_b). The tile max M = max_b m_b and the energy max
     // 2^(K - M) with K = max_b (m_b + log2 e_b) are reduced with shared-memory
     // atomics on order-preserving integer encodings while the tiles stream by.
-    const int et = threadIdx.x - 64;           // 0..127
+    const int grp = (warp - 2) >> 2;          // energy group of this warp
+    const int et = threadIdx.x - 64 - grp * 128;   // 0..127 within the group
     const int quarter = warp & 3;              // TMEM lane group of this warp
-    const int ew = et >> 5;                    // 0..3 index among energy warps
+    const int ew = et >> 5;                    // 0..3 index among the group's warps
+    const int bar_id = 1 + grp;                // the group's named barrier
     const unsigned lt = (1u << lane) - 1u;
     const float c = p.scale_log2;              // > 0 on this path
+    float2* stats = stats_all + grp * Nb;
+    uint32_t* selw = words_all + grp * 4 * nwords;
+    uint32_t* prw = selw + nwords;
+    int* selpre = reinterpret_cast<int*>(prw + nwords);
+    int* prpre = selpre + nwords;
+    uint32_t* sred = sred_all + 2 * grp;
+    int* totals = totals_all + 2 * grp;
     int tcount = 0;
     bool ok = true;   // after a failed wait the role keeps its barrier schedule but skips TMEM
     if (et == 0) {
       sred[0] = f2ord(-INFINITY);
       sred[1] = f2ord(-INFINITY);
     }
-    named_bar_sync(1, 128);
-    for (int w = blockIdx.x; w < total_work; w += gridDim.x) {
+    named_bar_sync(bar_id, 128);
+    for (int w = blockIdx.x + grp * gridDim.x; w < total_work; w += kGroups * gridDim.x) {
       const Item it = make_item(p, w);
       const long long row_base = ((long long)it.h * g.Nt + it.t) * Nb;
       for (int cc = 0; cc < p.n_chunks; ++cc) {
         for (int m = 0; m < it.n_mt; ++m) {
-          const int ts = tcount % kTmemSlots;
-          if (ok) ok = mbar_wait(smem_u32(&t_full[ts]), (tcount / kTmemSlots) & 1, wc);
+          const int ts = grp * kSlotsPerGroup + tcount % kSlotsPerGroup;
+          if (ok) ok = mbar_wait(smem_u32(&t_full[ts]), (tcount / kSlotsPerGroup) & 1, wc);
           ok = __all_sync(0xffffffffu, ok);   // the TMEM loads below are warp-collective
           ++tcount;
           tc_fence_after();
@@ -313,85 +332,90 @@ __global__ void __launch_bounds__(kThreads, 1)
               mb = st.x;
               eb = st.y;
             }
-            uint32_t sv[4][32];
+            // Two passes of 64 columns (registers: the CTA runs 10 warps, so a
+            // thread has at most 168); (m_b, e_b) is carried online between them.
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + ts * 128;
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4)
-              if (q4 * 32 < p.NC) tmem_ld32(taddr + q4 * 32, sv[q4]);
-            tmem_wait_ld();
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) reg_fence(sv[q4]);
             // Element masks are needed only for partially visible rows or a
             // narrow N-chunk; the decision is per item, so it never diverges
             // inside a warp. Lanes past the fully visible blocks compute on
             // whatever the tile holds and are simply not recorded.
             const bool masked = it.row_mask || p.NC < 128;
-            uint32_t vm[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
-            if (masked) {
-              const long long bstart = (long long)b * g.block_k;
+            const long long bstart = (long long)b * g.block_k;
 #pragma unroll 1
-              for (int q4 = 0; q4 < 4; ++q4) {
-                uint32_t bits = 0u;
-                for (int j = 0; j < 32; ++j) {
-                  const int col = q4 * 32 + j;
-                  bool v = col < p.NC;
-                  if (v && it.row_mask) {
-                    const int P = cc * p.NC + col;
-                    const long long row = (long long)it.t * g.tile_q + P % g.tile_q;
-                    v = row < g.valid_lq && bstart <= g.offset + row;
+            for (int hf = 0; hf < 2; ++hf) {
+              if (hf * 64 >= p.NC) break;
+              uint32_t sv[2][32];
+              tmem_ld32(taddr + hf * 64, sv[0]);
+              if (hf * 64 + 32 < p.NC) tmem_ld32(taddr + hf * 64 + 32, sv[1]);
+              tmem_wait_ld();
+              reg_fence(sv[0]);
+              reg_fence(sv[1]);
+              uint32_t vm[2] = {0xffffffffu, 0xffffffffu};
+              if (masked) {
+#pragma unroll 1
+                for (int q2 = 0; q2 < 2; ++q2) {
+                  uint32_t bits = 0u;
+                  for (int j = 0; j < 32; ++j) {
+                    const int col = hf * 64 + q2 * 32 + j;
+                    bool v = col < p.NC;
+                    if (v && it.row_mask) {
+                      const int P = cc * p.NC + col;
+                      const long long row = (long long)it.t * g.tile_q + P % g.tile_q;
+                      v = row < g.valid_lq && bstart <= g.offset + row;
+                    }
+                    bits |= v ? (1u << j) : 0u;
                   }
-                  bits |= v ? (1u << j) : 0u;
+                  vm[q2] = bits;
                 }
-                vm[q4] = bits;
               }
-            }
-            float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
-            if (!masked) {
+              float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+              if (!masked) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                m0 = fmaxf(m0, __uint_as_float(sv[0][j]));
-                m1 = fmaxf(m1, __uint_as_float(sv[1][j]));
-                m2 = fmaxf(m2, __uint_as_float(sv[2][j]));
-                m3 = fmaxf(m3, __uint_as_float(sv[3][j]));
-              }
-            } else {
+                for (int j = 0; j < 32; j += 2) {
+                  m0 = fmaxf(m0, __uint_as_float(sv[0][j]));
+                  m1 = fmaxf(m1, __uint_as_float(sv[0][j + 1]));
+                  m2 = fmaxf(m2, __uint_as_float(sv[1][j]));
+                  m3 = fmaxf(m3, __uint_as_float(sv[1][j + 1]));
+                }
+              } else {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                m0 = ((vm[0] >> j) & 1u) ? fmaxf(m0, __uint_as_float(sv[0][j])) : m0;
-                m1 = ((vm[1] >> j) & 1u) ? fmaxf(m1, __uint_as_float(sv[1][j])) : m1;
-                m2 = ((vm[2] >> j) & 1u) ? fmaxf(m2, __uint_as_float(sv[2][j])) : m2;
-                m3 = ((vm[3] >> j) & 1u) ? fmaxf(m3, __uint_as_float(sv[3][j])) : m3;
+                for (int j = 0; j < 32; j += 2) {
+                  m0 = ((vm[0] >> j) & 1u) ? fmaxf(m0, __uint_as_float(sv[0][j])) : m0;
+                  m1 = ((vm[0] >> (j + 1)) & 1u) ? fmaxf(m1, __uint_as_float(sv[0][j + 1])) : m1;
+                  m2 = ((vm[1] >> j) & 1u) ? fmaxf(m2, __uint_as_float(sv[1][j])) : m2;
+                  m3 = ((vm[1] >> (j + 1)) & 1u) ? fmaxf(m3, __uint_as_float(sv[1][j + 1])) : m3;
+                }
               }
-            }
-            const float mraw = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
-            const float mnew = fmaxf(mb, mraw * c);
-            // all lanes take the same path below (-inf maxima give ex2(-inf) = 0)
-            const float nm = mnew == -INFINITY ? 0.f : -mnew;
-            float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
-            if (!masked) {
+              const float mraw = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+              const float mnew = fmaxf(mb, mraw * c);
+              // all lanes take the same path below (-inf maxima give ex2(-inf) = 0)
+              const float nm = mnew == -INFINITY ? 0.f : -mnew;
+              float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
+              if (!masked) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                e0 += ex2(fmaf(__uint_as_float(sv[0][j]), c, nm));
-                e1 += ex2(fmaf(__uint_as_float(sv[1][j]), c, nm));
-                e2 += ex2(fmaf(__uint_as_float(sv[2][j]), c, nm));
-                e3 += ex2(fmaf(__uint_as_float(sv[3][j]), c, nm));
-              }
-            } else {
+                for (int j = 0; j < 32; j += 2) {
+                  e0 += ex2(fmaf(__uint_as_float(sv[0][j]), c, nm));
+                  e1 += ex2(fmaf(__uint_as_float(sv[0][j + 1]), c, nm));
+                  e2 += ex2(fmaf(__uint_as_float(sv[1][j]), c, nm));
+                  e3 += ex2(fmaf(__uint_as_float(sv[1][j + 1]), c, nm));
+                }
+              } else {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const float x0 = ex2(fmaf(__uint_as_float(sv[0][j]), c, nm));
-                const float x1 = ex2(fmaf(__uint_as_float(sv[1][j]), c, nm));
-                const float x2 = ex2(fmaf(__uint_as_float(sv[2][j]), c, nm));
-                const float x3 = ex2(fmaf(__uint_as_float(sv[3][j]), c, nm));
-                e0 += ((vm[0] >> j) & 1u) ? x0 : 0.f;
-                e1 += ((vm[1] >> j) & 1u) ? x1 : 0.f;
-                e2 += ((vm[2] >> j) & 1u) ? x2 : 0.f;
-                e3 += ((vm[3] >> j) & 1u) ? x3 : 0.f;
+                for (int j = 0; j < 32; j += 2) {
+                  const float x0 = ex2(fmaf(__uint_as_float(sv[0][j]), c, nm));
+                  const float x1 = ex2(fmaf(__uint_as_float(sv[0][j + 1]), c, nm));
+                  const float x2 = ex2(fmaf(__uint_as_float(sv[1][j]), c, nm));
+                  const float x3 = ex2(fmaf(__uint_as_float(sv[1][j + 1]), c, nm));
+                  e0 += ((vm[0] >> j) & 1u) ? x0 : 0.f;
+                  e1 += ((vm[0] >> (j + 1)) & 1u) ? x1 : 0.f;
+                  e2 += ((vm[1] >> j) & 1u) ? x2 : 0.f;
+                  e3 += ((vm[1] >> (j + 1)) & 1u) ? x3 : 0.f;
+                }
               }
-            }
-            if (mnew != -INFINITY) {
-              eb = eb * ex2(mb - mnew) + ((e0 + e1) + (e2 + e3));
-              mb = mnew;
+              if (mnew != -INFINITY) {
+                eb = eb * ex2(mb - mnew) + ((e0 + e1) + (e2 + e3));
+                mb = mnew;
+              }
             }
             if (bvalid) stats[b] = make_float2(mb, eb);
             if (cc == p.n_chunks - 1) {
@@ -413,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
       // ---- finalize: threshold, forcing, lists ----------------------------
-      named_bar_sync(1, 128);                      // stats, M and K complete
+      named_bar_sync(bar_id, 128);                 // stats, M and K complete
       const float Mx = ord2f(sred[0]);
       const float Kx = ord2f(sred[1]);
       const float emax = (Mx == -INFINITY || Kx == -INFINITY) ? 0.f : ex2(Kx - Mx);
@@ -438,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (p.mask != nullptr && b < Nb) p.mask[row_base + b] = (uint8_t)fin;
       }
-      named_bar_sync(1, 128);                      // words complete; M, K consumed
+      named_bar_sync(bar_id, 128);                 // words complete; M, K consumed
       if (et == 0) {
         sred[0] = f2ord(-INFINITY);
         sred[1] = f2ord(-INFINITY);
@@ -468,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           totals[1] = run_p;
         }
       }
-      named_bar_sync(1, 128);                      // prefixes complete
+      named_bar_sync(bar_id, 128);                 // prefixes complete
       if (p.sel_ids != nullptr) {
         const int nsel = totals[0], npr = totals[1];
         for (int base_b = ew * 32; base_b < Nb; base_b += 128) {
@@ -497,13 +521,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int D>
-size_t smem_bytes(int Nb) {
+size_t smem_bytes(int Nb, int k_stages) {
   const int nwords = (Nb + 31) / 32;
-  size_t s = 1024 + Cfg<D>::kOpBytes;
-  s += (size_t)Nb * 8 + (size_t)nwords * 16;
-  s += 8 + 8 * (2 * Cfg<D>::kQStages + 2 * Cfg<D>::kKStages + 2 * kTmemSlots + 1);
-  s += 8 + 8 * 4 + 8;
+  size_t s = 1024 + (size_t)Cfg<D>::kQStages * Cfg<D>::kQBytes + (size_t)k_stages * Cfg<D>::kKBytes;
+  s += (size_t)kGroups * ((size_t)Nb * 8 + (size_t)nwords * 16);
+  s += 8 + 8 * (2 * Cfg<D>::kQStages + 2 * Cfg<D>::kKStagesMax + 2 * kTmemSlots + 1);
+  s += 8 + 16 * kGroups + 8;
   return s;
+}
+
+// Largest pooled-K ring that fits next to the per-group statistics (0 if < 2).
+template <int D>
+int pick_k_stages(int Nb) {
+  for (int ks = Cfg<D>::kKStagesMax; ks >= 2; --ks)
+    if (smem_bytes<D>(Nb, ks) <= (size_t)kSmemLimit) return ks;
+  return 0;
 }
 
 }  // namespace
@@ -513,6 +545,7 @@ bool select_tc_supported(const SelectGeom& g, int dt) {
   if (!(g.scale > 0.f)) return false;
   if (g.D != 64 && g.D != 128) return false;
   if (g.Nb > kMaxNb || g.Nb <= 0) return false;
+  if ((g.D == 64 ? pick_k_stages<64>(g.Nb) : pick_k_stages<128>(g.Nb)) == 0) return false;
   const int R = g.G * g.tile_q;
   if (R >= 128) {
     if (R % 128) return false;
@@ -560,13 +593,15 @@ cudaError_t launch_select_tc(const SelectTcArgs& a, const void* q, const void* p
   grid = max(1, min(grid, total));
   cudaError_t e;
   if (g.D == 64) {
-    const size_t smem = smem_bytes<64>(g.Nb);
+    p.k_stages = pick_k_stages<64>(g.Nb);
+    const size_t smem = smem_bytes<64>(g.Nb, p.k_stages);
     e = cudaFuncSetAttribute(select_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem);
     if (e != cudaSuccess) return e;
     select_tc_kernel<64><<<grid, kThreads, smem, stream>>>(tq, tk, p);
   } else {
-    const size_t smem = smem_bytes<128>(g.Nb);
+    p.k_stages = pick_k_stages<128>(g.Nb);
+    const size_t smem = smem_bytes<128>(g.Nb, p.k_stages);
     e = cudaFuncSetAttribute(select_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem);
     if (e != cudaSuccess) return e;
