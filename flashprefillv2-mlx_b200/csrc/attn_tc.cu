@@ -12,9 +12,16 @@
 //   S[128x128] = Q . K^T          tcgen05.mma SS, fp32 in TMEM (double buffered)
 //   P = 2^(S*c - m)               softmax warps: TMEM -> regs -> bf16/f16 P back
 //                                 into the same TMEM columns
-//   O[128xD] += P . V             tcgen05.mma TS (A = P from TMEM, B = V MN-major)
-// The running max is rescaled lazily: O in TMEM is only rescaled when a row's
-// max grows by more than 2^8, which leaves the final O/l unchanged.
+//   O_h[128xD] += P_h . V_h       tcgen05.mma TS (A = P from TMEM, B = V MN-major)
+// Each 128-key S tile is split into two 64-key halves h with fully separate
+// online-softmax state: a half has its own running max m_h, sum l_h and
+// accumulator O_h in TMEM (TMEM = O_0 | O_1 | S buffer 0 | S buffer 1, 4 x 128
+// columns). The two halves of a row are combined once per work item:
+//   out = (2^(m_0-m) O_0 + 2^(m_1-m) O_1) / (2^(m_0-m) l_0 + 2^(m_1-m) l_1),
+// m = max(m_0, m_1), which equals the single online softmax over all keys.
+// So the two warps that share a row never exchange anything per KV item.
+// Each running max is rescaled lazily: O_h is only rescaled when m_h grows by
+// more than 2^8, which leaves the final result unchanged.
 //
 // Pooled correction: instead of gathering the pruned blocks' pooled rows, the
 // producer streams contiguous 128-row tiles of the head's pooled K/V with TMA
@@ -29,8 +36,9 @@
 //              loads Q / K / V / pooled tiles with TMA (no multicast);
 //   warp 1     MMA issuer;
 //   warps 2-9  softmax and the output epilogue: two warps per TMEM lane
-//              quarter (thread = query row), each owning 64 of the 128 keys
-//              of an S tile and half of O's columns.
+//              quarter (thread = query row), each owning one 64-key half of
+//              every S tile and its accumulator O_h; in the epilogue each
+//              writes half of the output columns.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -42,7 +50,10 @@ constexpr int kThreads = 320;   // producer, MMA, 8 softmax warps
 constexpr int kStages = 2;      // K/V tiles and S buffers
 constexpr int kRecs = 8;        // item records in flight
 constexpr int kTmemCols = 512;
-constexpr float kRescaleThreshold = 8.0f;   // log2 units
+// Lazy-rescale threshold in log2 units: P = 2^(x - m_h) stays below 2^T, which
+// the 16-bit P of the PV product represents (fp16 max 65504 < 2^16).
+template <int DT> struct RescaleT { static constexpr float value = 16.0f; };
+template <> struct RescaleT<DT_F16> { static constexpr float value = 15.0f; };
 constexpr int kMaskWordsMax = 64;           // pooled-entry mask of one work item (Nb <= 2048)
 
 enum : int { KIND_SEL = 0, KIND_POOL = 1, KIND_CORR = 2, KIND_EMPTY = 3, KIND_DONE = 4 };
@@ -60,8 +71,8 @@ template <int D>
 struct Cfg {
   static constexpr int kHalves = D / 64;
   static constexpr int kTileBytes = 128 * D * 2;   // Q, K or V tile
-  static constexpr int kOCol = 0;                  // O accumulator columns [0, D)
-  static constexpr int kSCol = D;                  // S buffers at D, D + 128
+  static constexpr int kOCol = 0;                  // O_h at columns [128 h, 128 h + D)
+  static constexpr int kSCol = 256;                // S buffers at 256, 384
 };
 
 struct Params {
@@ -120,8 +131,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* after_tiles = gbase + (2 + 2 * kStages) * C::kTileBytes;
   Rec* recs = reinterpret_cast<Rec*>(after_tiles);                // [kRecs]
   uint32_t* pmask = reinterpret_cast<uint32_t*>(recs + kRecs);    // producer-private [64]
-  float* pmax = reinterpret_cast<float*>(pmask + kMaskWordsMax);  // [2 parity][2 half][128]
-  float* lsum = pmax + 2 * 2 * 128;                                // [2 parity][2 half][128]
+  float* xm = reinterpret_cast<float*>(pmask + kMaskWordsMax);    // [2 parity][2 half][128] m_h
+  float* lsum = xm + 2 * 2 * 128;                                  // [2 parity][2 half][128] l_h
   uint64_t* bars = reinterpret_cast<uint64_t*>(lsum + 2 * 2 * 128);
   uint64_t* q_full = bars;              // [2]
   uint64_t* q_empty = q_full + 2;       // [2]
@@ -133,13 +144,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* v_empty = v_full + kStages;
   uint64_t* s_full = v_empty + kStages;
   uint64_t* s_free = s_full + kStages;
-  uint64_t* p_full = s_free + kStages;
-  uint64_t* pv_done = p_full + kStages;  // [1]
+  uint64_t* p_full = s_free + kStages;  // [kStages][2 half] (4 warps each)
+  uint64_t* pv_done = p_full + 2 * kStages;  // [1]
   uint64_t* o_full = pv_done + 1;        // [1]
   uint64_t* o_free = o_full + 1;         // [1]
   uint64_t* drain = o_free + 1;          // [1]
-  uint64_t* xbar = drain + 1;            // [4] row-max exchange of a warp pair
-  uint64_t* lbar = xbar + 4;             // [4] row-sum exchange of a warp pair
+  uint64_t* lbar = drain + 1;            // [4] epilogue (m_h, l_h) exchange of a warp pair
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(lbar + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -162,16 +172,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&v_empty[i]), 1);
       mbar_init(smem_u32(&s_full[i]), 1);
       mbar_init(smem_u32(&s_free[i]), 1);
-      mbar_init(smem_u32(&p_full[i]), 8);
+      mbar_init(smem_u32(&p_full[2 * i]), 4);
+      mbar_init(smem_u32(&p_full[2 * i + 1]), 4);
     }
     mbar_init(smem_u32(pv_done), 1);
     mbar_init(smem_u32(o_full), 1);
     mbar_init(smem_u32(o_free), 8);
     mbar_init(smem_u32(drain), 1);
-    for (int i = 0; i < 4; ++i) {
-      mbar_init(smem_u32(&xbar[i]), 2);
-      mbar_init(smem_u32(&lbar[i]), 2);
-    }
+    for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&lbar[i]), 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -432,20 +440,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_pv = [&](int n) -> bool {
         const int st = n % kStages;
         const uint32_t par = (n / kStages) & 1;
-        if (!mbar_wait(smem_u32(&p_full[st]), par, wc)) return false;
         if (!mbar_wait(smem_u32(&v_full[st]), par, wc)) return false;
         if (need_ofree) {
           if (!mbar_wait(smem_u32(o_free), (wi - 1) & 1, wc)) return false;
           need_ofree = false;
         }
-        tc_fence_after();
-        const uint32_t o_tmem = tmem_base + C::kOCol;
-        const uint32_t p_tmem = tmem_base + C::kSCol + st * 128;
+        const uint32_t s_tmem = tmem_base + C::kSCol + st * 128;
         const uint32_t vst = v_smem + st * C::kTileBytes;
+        // O_h += P_h V_h, each half as soon as its four softmax warps are done;
+        // P_h (64 keys, 16-bit pairs) sits in the first 32 of its S columns.
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t bdesc = sw128_desc(vst + kk * 2048, 16384, 1024);
-          umma_ts(o_tmem, p_tmem + kk * 8, bdesc, p.idesc_pv, (first_pv && kk == 0) ? 0u : 1u);
+        for (int h = 0; h < 2; ++h) {
+          if (!mbar_wait(smem_u32(&p_full[2 * st + h]), par, wc)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t bdesc = sw128_desc(vst + (4 * h + kk) * 2048, 16384, 1024);
+            umma_ts(tmem_base + C::kOCol + h * 128, s_tmem + 64 * h + kk * 8, bdesc, p.idesc_pv,
+                    (first_pv && kk == 0) ? 0u : 1u);
+          }
         }
         first_pv = false;
         umma_commit(smem_u32(&v_empty[st]));
@@ -513,14 +526,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ======================= softmax + epilogue ============================
     // Eight warps: warp w serves TMEM lane quarter w % 4 (query rows
-    // 32*(w%4) .. +31) and column half (w - 2) / 4 of every S tile (64 keys).
-    // The two warps of a quarter combine their row maxima through shared
-    // memory (a 2-arrival mbarrier per quarter), keep separate partial row sums, and rescale /
-    // store their own half of O's columns.
+    // 32*(w%4) .. +31) and key half h = (w - 2) / 4 of every S tile (64 keys),
+    // with its own running max m_h, sum l_h and accumulator O_h.
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;           // 0: columns [0, 64), 1: [64, 128)
+    const int half = (warp - 2) >> 2;           // 0: keys [0, 64), 1: [64, 128)
     const int r = quarter * 32 + lane;          // row of the 128-row chunk
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t o_tmem = tmem_base + lane_off + C::kOCol + half * 128;
     const float c2 = a.scale_log2;
     int icount = 0, kv = 0, wi = 0;
     bool ok = true;
@@ -528,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int gq = 0;
     long long row = 0, position = 0;
     bool row_valid = false;
-    float m_used = kFiniteMin, l = 0.f;   // l: this warp's half of the row sum
+    float m_used = kFiniteMin, l = 0.f;   // this half's running max and sum
     int pv_wi = 0;
     while (ok) {
       const int ri = icount % kRecs;
@@ -558,10 +570,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t s_tmem = tmem_base + lane_off + C::kSCol + st * 128;
+        const uint32_t s_tmem = tmem_base + lane_off + C::kSCol + st * 128 + half * 64;
         uint32_t s[2][32];
-        tmem_ld32(s_tmem + half * 64, s[0]);
-        tmem_ld32(s_tmem + half * 64 + 32, s[1]);
+        tmem_ld32(s_tmem, s[0]);
+        tmem_ld32(s_tmem + 32, s[1]);
         tmem_wait_ld();
         reg_fence(s[0]);
         reg_fence(s[1]);
@@ -594,36 +606,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             vm1 = nv1 >= 32 ? 0xffffffffu : (nv1 <= 0 ? 0u : ((1u << nv1) - 1u));
           }
         }
-        // partial row max over valid raw scores (c2 > 0 keeps the order)
-        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-        if (full) {
+        // x = s * c2 + bias in the log2 domain; a masked entry takes finite_min,
+        // exactly as the reference kernel masks its logits. One exp loop serves
+        // every kind of item; only partially valid warps pay for the selects.
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            mx0 = fmaxf(mx0, __uint_as_float(s[0][j]));
-            mx1 = fmaxf(mx1, __uint_as_float(s[0][j + 1]));
-            mx2 = fmaxf(mx2, __uint_as_float(s[1][j]));
-            mx3 = fmaxf(mx3, __uint_as_float(s[1][j + 1]));
-          }
-        } else {
+        for (int j = 0; j < 32; ++j) {
+          s[0][j] = __float_as_uint(fmaf(__uint_as_float(s[0][j]), c2, bias));
+          s[1][j] = __float_as_uint(fmaf(__uint_as_float(s[1][j]), c2, bias));
+        }
+        if (!full) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            mx0 = ((vm0 >> j) & 1u) ? fmaxf(mx0, __uint_as_float(s[0][j])) : mx0;
-            mx1 = ((vm0 >> (j + 1)) & 1u) ? fmaxf(mx1, __uint_as_float(s[0][j + 1])) : mx1;
-            mx2 = ((vm1 >> j) & 1u) ? fmaxf(mx2, __uint_as_float(s[1][j])) : mx2;
-            mx3 = ((vm1 >> (j + 1)) & 1u) ? fmaxf(mx3, __uint_as_float(s[1][j + 1])) : mx3;
+          for (int j = 0; j < 32; ++j) {
+            s[0][j] = ((vm0 >> j) & 1u) ? s[0][j] : __float_as_uint(kFiniteMin);
+            s[1][j] = ((vm1 >> j) & 1u) ? s[1][j] : __float_as_uint(kFiniteMin);
           }
         }
-        const float mraw_half = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-        pmax[((kv & 1) * 2 + half) * 128 + r] = mraw_half;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&xbar[quarter]));
-        ok = mbar_wait(smem_u32(&xbar[quarter]), kv & 1, wc);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-        const float mraw = fmaxf(mraw_half, pmax[((kv & 1) * 2 + (half ^ 1)) * 128 + r]);
-        const float mt = mraw == -INFINITY ? kFiniteMin : fmaf(mraw, c2, bias);
+        float mx0 = kFiniteMin, mx1 = kFiniteMin, mx2 = kFiniteMin, mx3 = kFiniteMin;
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          mx0 = fmaxf(mx0, __uint_as_float(s[0][j]));
+          mx1 = fmaxf(mx1, __uint_as_float(s[0][j + 1]));
+          mx2 = fmaxf(mx2, __uint_as_float(s[1][j]));
+          mx3 = fmaxf(mx3, __uint_as_float(s[1][j + 1]));
+        }
+        const float mt = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
         const float m_new = fmaxf(m_used, mt);
-        const bool need = m_new > m_used + kRescaleThreshold ||
+        const bool need = m_new > m_used + RescaleT<DT>::value ||
                           (m_used == kFiniteMin && m_new > kFiniteMin);
         if (__any_sync(0xffffffffu, need)) {
           const float f = need ? ex2(m_used - m_new) : 1.f;
@@ -632,107 +640,98 @@ __global__ void __launch_bounds__(kThreads, 1)
             l *= f;
           }
           if (pv_wi > 0) {
-            // O holds PVs of this work item: wait for the latest one, rescale this
-            // warp's half of the row's columns.
+            // O_h holds PVs of this work item: wait for the latest one, rescale.
             ok = mbar_wait(smem_u32(pv_done), (kv - 1) & 1, wc);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc_fence_after();
-#pragma unroll
-            for (int dc = 0; dc < D / 64; ++dc) {
+#pragma unroll 1
+            for (int dc = 0; dc < D / 32; ++dc) {
               uint32_t o[32];
-              const uint32_t oaddr = tmem_base + lane_off + C::kOCol + half * (D / 2) + dc * 32;
-              tmem_ld32(oaddr, o);
+              tmem_ld32(o_tmem + dc * 32, o);
               tmem_wait_ld();
               reg_fence(o);
 #pragma unroll
               for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * f);
-              tmem_st32(oaddr, o);
+              tmem_st32(o_tmem + dc * 32, o);
             }
             tmem_wait_st();
           }
         }
-        // P = 2^(s*c2 + bias - m); a masked entry weighs 2^(finite_min - m), i.e.
-        // 1 while the row has seen nothing but masked entries, else 0.
-        const float neg_m = bias - m_used;
-        const float masked_p = (m_used == kFiniteMin) ? 1.f : 0.f;
+        // P = 2^(x - m): a masked entry (x = finite_min) weighs 1 while the half
+        // has seen nothing but masked entries (m = finite_min), else 0.
         float rs0 = 0.f, rs1 = 0.f, rs2 = 0.f, rs3 = 0.f;
         uint32_t pk[32];
-        if (full) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            const float p0 = ex2(fmaf(__uint_as_float(s[0][j]), c2, neg_m));
-            const float p1 = ex2(fmaf(__uint_as_float(s[0][j + 1]), c2, neg_m));
-            const float p2 = ex2(fmaf(__uint_as_float(s[1][j]), c2, neg_m));
-            const float p3 = ex2(fmaf(__uint_as_float(s[1][j + 1]), c2, neg_m));
-            rs0 += p0;
-            rs1 += p1;
-            rs2 += p2;
-            rs3 += p3;
-            pk[j >> 1] = pack2<DT>(p0, p1);
-            pk[16 + (j >> 1)] = pack2<DT>(p2, p3);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            float p0 = ex2(fmaf(__uint_as_float(s[0][j]), c2, neg_m));
-            float p1 = ex2(fmaf(__uint_as_float(s[0][j + 1]), c2, neg_m));
-            float p2 = ex2(fmaf(__uint_as_float(s[1][j]), c2, neg_m));
-            float p3 = ex2(fmaf(__uint_as_float(s[1][j + 1]), c2, neg_m));
-            p0 = ((vm0 >> j) & 1u) ? p0 : masked_p;
-            p1 = ((vm0 >> (j + 1)) & 1u) ? p1 : masked_p;
-            p2 = ((vm1 >> j) & 1u) ? p2 : masked_p;
-            p3 = ((vm1 >> (j + 1)) & 1u) ? p3 : masked_p;
-            rs0 += p0;
-            rs1 += p1;
-            rs2 += p2;
-            rs3 += p3;
-            pk[j >> 1] = pack2<DT>(p0, p1);
-            pk[16 + (j >> 1)] = pack2<DT>(p2, p3);
-          }
+        for (int j = 0; j < 32; j += 2) {
+          const float p0 = ex2(__uint_as_float(s[0][j]) - m_used);
+          const float p1 = ex2(__uint_as_float(s[0][j + 1]) - m_used);
+          const float p2 = ex2(__uint_as_float(s[1][j]) - m_used);
+          const float p3 = ex2(__uint_as_float(s[1][j + 1]) - m_used);
+          rs0 += p0;
+          rs1 += p1;
+          rs2 += p2;
+          rs3 += p3;
+          pk[j >> 1] = pack_p<DT>(p0, p1);
+          pk[16 + (j >> 1)] = pack_p<DT>(p2, p3);
         }
         l += (rs0 + rs1) + (rs2 + rs3);
-        // P of keys [64 half, +64) -> TMEM columns [32 half, +32) of the S buffer
-        tmem_st32(s_tmem + half * 32, pk);
+        // P_h -> the first 32 columns of this half's own S columns (already read)
+        tmem_st32(s_tmem, pk);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&p_full[st]));
+        if (lane == 0) mbar_arrive(smem_u32(&p_full[2 * st + half]));
         ++kv;
         ++pv_wi;
       }
       if (rec.flags & 2) {
-        // ---- epilogue: O / l -> out ----------------------------------------
+        // ---- epilogue: combine the halves, out = sum_h a_h O_h / sum_h a_h l_h
+        xm[((wi & 1) * 2 + half) * 128 + r] = m_used;
         lsum[((wi & 1) * 2 + half) * 128 + r] = l;
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&lbar[quarter]));
         ok = mbar_wait(smem_u32(&lbar[quarter]), wi & 1, wc);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
-        const float lrow = l + lsum[((wi & 1) * 2 + (half ^ 1)) * 128 + r];
+        const float m_o = xm[((wi & 1) * 2 + (half ^ 1)) * 128 + r];
+        const float l_o = lsum[((wi & 1) * 2 + (half ^ 1)) * 128 + r];
+        const float m_row = fmaxf(m_used, m_o);
+        const float a_me = ex2(m_used - m_row), a_o = ex2(m_o - m_row);
+        const float lrow = l * a_me + l_o * a_o;
+        const float inv = (pv_wi > 0 && lrow > 0.f) ? 1.f / lrow : 0.f;
+        const float w_lo = (half == 0 ? a_me : a_o) * inv;   // weight of O_0
+        const float w_hi = (half == 0 ? a_o : a_me) * inv;   // weight of O_1
         ok = mbar_wait(smem_u32(o_full), wi & 1, wc);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
         using T = typename Elem<DT>::T;
+        // this warp writes output columns [half * D/2, half * D/2 + D/2)
         T* out = reinterpret_cast<T*>(a.out) +
                  (((long long)(ck.h * a.G + gq)) * a.Lq_pad + row) * D + half * (D / 2);
-        const float inv = pv_wi > 0 ? 1.f / lrow : 0.f;
-#pragma unroll
+        const uint32_t o0 = tmem_base + lane_off + C::kOCol + half * (D / 2);
+#pragma unroll 1
         for (int dc = 0; dc < D / 64; ++dc) {
-          uint32_t o[32];
+          uint32_t x0[32], x1[32];
           if (pv_wi > 0) {
-            tmem_ld32(tmem_base + lane_off + C::kOCol + half * (D / 2) + dc * 32, o);
+            tmem_ld32(o0 + dc * 32, x0);
+            tmem_ld32(o0 + 128 + dc * 32, x1);
             tmem_wait_ld();
-            reg_fence(o);
+            reg_fence(x0);
+            reg_fence(x1);
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) o[j] = 0u;
+            for (int j = 0; j < 32; ++j) x0[j] = x1[j] = 0u;
           }
           uint32_t packed[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            packed[j] = pack2<DT>(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
+          for (int j = 0; j < 16; ++j) {
+            const float v0 = __uint_as_float(x0[2 * j]) * w_lo + __uint_as_float(x1[2 * j]) * w_hi;
+            const float v1 =
+                __uint_as_float(x0[2 * j + 1]) * w_lo + __uint_as_float(x1[2 * j + 1]) * w_hi;
+            packed[j] = pack2<DT>(v0, v1);
+          }
           uint4* dst = reinterpret_cast<uint4*>(out + dc * 32);
 #pragma unroll
           for (int j = 0; j < 4; ++j)
@@ -755,7 +754,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int D>
 size_t smem_bytes() {
   return 1024 + (size_t)(2 + 2 * kStages) * Cfg<D>::kTileBytes + sizeof(Rec) * kRecs +
-         4 * kMaskWordsMax + 4 * (4 * 128 + 4 * 128) + 8 * (4 + 2 * kRecs + 7 * kStages + 12) + 16;
+         4 * kMaskWordsMax + 4 * (4 * 128 + 4 * 128) + 8 * (4 + 2 * kRecs + 8 * kStages + 8) + 16;
 }
 
 }  // namespace

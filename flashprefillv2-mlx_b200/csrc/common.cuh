@@ -74,6 +74,22 @@ template <> __device__ __forceinline__ float2 unpack2<DT_F16>(uint32_t v) {
   return __half22float2(h);
 }
 
+// Packing of softmax probabilities p in [0, 2^16] for the P.V MMA. For bf16 the
+// conversion is done on the integer units (round half up on the 16 dropped
+// bits, then a byte permute), which keeps it off the pipe that evaluates ex2;
+// it differs from round-to-nearest-even only on exact ties.
+template <int DT> __device__ __forceinline__ uint32_t pack_p(float lo, float hi);
+template <> __device__ __forceinline__ uint32_t pack_p<DT_BF16>(float lo, float hi) {
+  const uint32_t a = __float_as_uint(lo) + 0x8000u;
+  const uint32_t b = __float_as_uint(hi) + 0x8000u;
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+template <> __device__ __forceinline__ uint32_t pack_p<DT_F16>(float lo, float hi) {
+  return pack2<DT_F16>(lo, hi);
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
