@@ -43,6 +43,13 @@ METRIC = "sparse prefill-attn ms/layer & TFLOP/s (retained) at 64k; % bf16 peak;
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
+# DRAM bytes per launch of the dominant kernels, from one ncu capture of the
+# full-size single-GPU workload (dram__bytes_read.sum + dram__bytes_write.sum;
+# profiles/dram_traffic_c3.md has the command and the per-kernel split).
+NCU_TRAFFIC_BYTES = {
+    "c3": {"attention": 2.84e9 + 500.12e6, "index_stage": 268.51e6 + 1.59e6 + 537.55e6 + 57.61e6},
+}
+
 CONFIGS = {
     # name: (length, Hq, Hkv, head_dim, dtype, alpha)
     "c3": (65536, 32, 8, 128, torch.bfloat16, 0.1),
@@ -211,7 +218,9 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="c3")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["c4"], default="c3",
+                    help="c4: chunked 64k prefill through a random-init Qwen3-4B-architecture model")
+    ap.add_argument("--c4-layers", type=int, default=36, help="decoder layers of the c4 model")
     ap.add_argument("--no-corr", action="store_true", help="mean correction off")
     ap.add_argument("--alpha", type=float, default=None)
     ap.add_argument("--no-e2e", action="store_true")
@@ -237,8 +246,144 @@ def dist_setup(n: int):
     return rank, world, local
 
 
+# ---------------------------------------------------------------------------
+# c4: chunked prefill through a random-init Qwen3-4B-architecture model
+# ---------------------------------------------------------------------------
+
+
+def _qwen3_weights(dev, layers, seed=0):
+    """Random bf16 weights ~ N(0, 0.02) of the Qwen3-4B architecture (hidden 2560,
+    32 Q / 8 KV heads of 128, SwiGLU 9728, RMSNorm with per-head q/k norms)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+
+    def w(*shape):
+        return (torch.randn(*shape, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+
+    H, I, HQ, HKV, D, V = 2560, 9728, 32, 8, 128, 151936
+    ones = lambda n: torch.ones(n, device=dev, dtype=torch.bfloat16)  # noqa: E731
+    blocks = [dict(ln1=ones(H), wq=w(HQ * D, H), wk=w(HKV * D, H), wv=w(HKV * D, H), qn=ones(D),
+                   kn=ones(D), wo=w(H, HQ * D), ln2=ones(H), wg=w(I, H), wu=w(I, H), wd=w(H, I))
+              for _ in range(layers)]
+    return dict(embed=w(V, H), blocks=blocks, norm=ones(H), lm_head=w(V, H))
+
+
+def _rope(x, pos, theta=1e6):
+    d = x.shape[-1]
+    inv = 1.0 / (theta ** (torch.arange(0, d, 2, device=x.device, dtype=torch.float32) / d))
+    ang = pos[:, None].float() * inv[None]
+    cos, sin = ang.cos(), ang.sin()
+    x1, x2 = x[..., : d // 2].float(), x[..., d // 2:].float()
+    c, s_ = cos[:, None, :], sin[:, None, :]
+    return torch.cat([x1 * c - x2 * s_, x2 * c + x1 * s_], dim=-1).to(x.dtype)
+
+
+def _qwen3_prefill(weights, ids, chunk, dense_expand_kv):
+    """Chunked prefill against a growing KV cache; returns last-token logits.
+
+    Attention is a plain ``torch.nn.functional.scaled_dot_product_attention``
+    call: ``is_causal=True`` for the first chunk and a bottom-right
+    ``causal_lower_right`` bias once the cache is longer than the chunk (the
+    form the FPV2 hook claims). The stock dense path cannot combine that bias
+    with ``enable_gqa``, so the dense baseline repeats K/V heads instead."""
+    import torch.nn.functional as F
+    from torch.nn.attention.bias import causal_lower_right
+
+    dev = ids.device
+    L = ids.numel()
+    HQ, HKV, D = 32, 8, 128
+    layers = len(weights["blocks"])
+    kc = [torch.empty((HKV, L, D), device=dev, dtype=torch.bfloat16) for _ in range(layers)]
+    vc = [torch.empty((HKV, L, D), device=dev, dtype=torch.bfloat16) for _ in range(layers)]
+    x = None
+    for off in range(0, L, chunk):
+        T = min(chunk, L - off)
+        pos = torch.arange(off, off + T, device=dev)
+        x = weights["embed"][ids[off:off + T]]
+        for li, b in enumerate(weights["blocks"]):
+            h = F.rms_norm(x, (x.shape[-1],), b["ln1"], eps=1e-6)
+            q = F.rms_norm((h @ b["wq"].T).view(T, HQ, D), (D,), b["qn"], eps=1e-6)
+            k = F.rms_norm((h @ b["wk"].T).view(T, HKV, D), (D,), b["kn"], eps=1e-6)
+            v = (h @ b["wv"].T).view(T, HKV, D)
+            q, k = _rope(q, pos), _rope(k, pos)
+            kc[li][:, off:off + T] = k.transpose(0, 1)
+            vc[li][:, off:off + T] = v.transpose(0, 1)
+            q4 = q.transpose(0, 1)[None]
+            k4, v4 = kc[li][None, :, :off + T], vc[li][None, :, :off + T]
+            if off == 0:
+                o = F.scaled_dot_product_attention(q4, k4, v4, is_causal=True, enable_gqa=True,
+                                                   scale=D ** -0.5)
+            elif dense_expand_kv:
+                o = F.scaled_dot_product_attention(
+                    q4, k4.repeat_interleave(HQ // HKV, dim=1), v4.repeat_interleave(HQ // HKV, dim=1),
+                    attn_mask=causal_lower_right(T, off + T), scale=D ** -0.5)
+            else:
+                o = F.scaled_dot_product_attention(q4, k4, v4, attn_mask=causal_lower_right(T, off + T),
+                                                   enable_gqa=True, scale=D ** -0.5)
+            x = x + o[0].transpose(0, 1).reshape(T, HQ * D) @ b["wo"].T
+            h = F.rms_norm(x, (x.shape[-1],), b["ln2"], eps=1e-6)
+            x = x + (F.silu(h @ b["wg"].T) * (h @ b["wu"].T)) @ b["wd"].T
+    last = F.rms_norm(x[-1:], (x.shape[-1],), weights["norm"], eps=1e-6)
+    return (last @ weights["lm_head"].T).float()
+
+
+def c4_prefill(args) -> int:
+    """a 65536-token prompt in 2048-token chunks, total_tokens
+    known (dense tail only at the last chunk), FPV2 hook vs the stock dense path."""
+    import fpv2
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L, chunk = 65536, 2048
+    weights = _qwen3_weights(dev, args.c4_layers)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    ids = torch.randint(0, 151936, (L,), device=dev, generator=g)
+    times = {}
+    logits = {}
+    with torch.no_grad():
+        for mode in ("fpv2", "dense"):
+            if mode == "fpv2":
+                fpv2.enable(fpv2.FPV2Config(alpha=0.1), min_tokens=4096, collect_stats=True,
+                            total_tokens=L)
+            # warm-up on a short prompt (kernels, cuBLAS handles)
+            _qwen3_prefill(weights, ids[:2 * chunk], chunk, mode == "dense")
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(0) as clocks:
+                e0.record()
+                logits[mode] = _qwen3_prefill(weights, ids, chunk, mode == "dense")
+                e1.record()
+                torch.cuda.synchronize()
+            times[mode] = e0.elapsed_time(e1) / 1000.0
+            if mode == "fpv2":
+                sparsity = fpv2.block_sparsity()
+                fpv2.disable()
+    a, b = logits["fpv2"], logits["dense"]
+    cos = float(torch.nn.functional.cosine_similarity(a, b).item())
+    line = {
+        "metric": "chunked 64k prefill tokens/s through a Qwen3-4B-architecture model (FPV2 hook)",
+        "value": round(L / times["fpv2"], 1), "unit": "tokens/s", "n_gpus": 1, "steps": 1,
+        "warmup": 1, "ms_per_step": round(1000 * times["fpv2"], 2), "higher_is_better": True,
+        "scaling": "none", "vs_baseline": None, "dtype": "bf16",
+        "data": "random-init weights ~ N(0, 0.02), token ids uniform over the 151936 vocab (seed 1)",
+        "config": {"workload": f"c4: {L} tokens in {chunk}-token chunks, total_tokens={L}, "
+                               f"{args.c4_layers} layers, alpha=0.1, min_tokens=4096",
+                   "dense_prefill_s": round(times["dense"], 3),
+                   "fpv2_prefill_s": round(times["fpv2"], 3),
+                   "speedup_vs_dense": round(times["dense"] / times["fpv2"], 3),
+                   "block_sparsity": round(sparsity, 4),
+                   "last_token_logit_cosine_vs_dense": round(cos, 5)},
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
+    if args.config == "c4":
+        return c4_prefill(args)
     length, Hq, Hkv, D, dtype, alpha = CONFIGS[args.config]
     if args.alpha is not None:
         alpha = args.alpha
@@ -418,6 +563,7 @@ def main(argv=None) -> int:
         peak_t = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
         dense_flops = 4.0 * D * Hq * length * (length + 1) / 2
         value = flops_layer / (ms_per_step * 1e-3) / 1e12
+        traffic = NCU_TRAFFIC_BYTES.get(args.config, {}) if world == 1 else {}
         line = {
             "metric": METRIC,
             "value": round(value, 3),
@@ -455,13 +601,15 @@ def main(argv=None) -> int:
             "roofline": {
                 "bound": "tensor", "kernel": "attn_tc_kernel (sparse attention)",
                 "achieved": round(attn_tflops, 1), "peak": peak_t, "unit": "TFLOP/s",
-                "frac": round(attn_tflops / peak_t, 4), "traffic": None,
+                "frac": round(attn_tflops / peak_t, 4), "traffic": traffic.get("attention"),
+                "traffic_unit": "bytes per launch (ncu, DRAM read + write)",
                 "peak_source": f"{peak_src} bf16_tflops_sustained",
             },
             "roofline_index_stage": {
                 "bound": "hbm", "kernel": "pool_vec_kernel + select_tc_kernel",
                 "achieved": round(idx_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": round(idx_gbs / peaks["hbm_gbs"], 4), "traffic": None,
+                "frac": round(idx_gbs / peaks["hbm_gbs"], 4), "traffic": traffic.get("index_stage"),
+                "traffic_unit": "bytes per launch pair (ncu, DRAM read + write)",
                 "algorithmic_bytes": idx_bytes_rank, "peak_source": f"{peak_src} hbm_gbs",
             },
             "cpu_baseline": cpu,

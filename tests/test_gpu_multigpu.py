@@ -1,0 +1,84 @@
+"""Head-parallel FPV2 on two GPUs (NCCL) equals the single-GPU layer.
+
+Each rank runs the index stage and the sparse attention on its KV-head shard
+(and the matching query heads); one NCCL all-gather reassembles the output.
+Every selection reduction, list and K/V read of the path belongs to one KV
+head, so the sharded layer must reproduce the single-GPU layer bit for bit.
+Skipped unless at least two GPUs are visible.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import traceback
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs(length: int, hq: int, hkv: int):
+    from tests.synthetic import topic_qkv
+
+    q, k, v = topic_qkv(length=length, query_heads=hq, kv_heads=hkv, seed=21, dtype=torch.bfloat16)
+    return q[None], k[None], v[None]
+
+
+def _worker(rank: int, world: int, port: int, length: int, hq: int, hkv: int, queue) -> None:
+    import torch.distributed as dist
+
+    try:
+        import fpv2
+        from fpv2.shard import head_parallel_sdpa, head_shard, shard_inputs
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                                device_id=dev)
+        q, k, v = _inputs(length, hq, hkv)
+        sh = head_shard(hq, hkv, world, rank)
+        ql, kl, vl = (t.to(dev) for t in shard_inputs(q, k, v, sh))
+        cfg = fpv2.FPV2Config(alpha=0.1)
+        out = head_parallel_sdpa(ql, kl, vl, scale=128 ** -0.5, config=cfg)
+        torch.cuda.synchronize(dev)
+        if rank == 0:
+            ref = fpv2.fpv2_sdpa(q.to(dev), k.to(dev), v.to(dev), scale=128 ** -0.5, config=cfg)
+            torch.cuda.synchronize(dev)
+            diff = (out.float() - ref.float()).abs().max().item()
+            queue.put((rank, f"maxdiff {diff}"))
+        else:
+            queue.put((rank, "ok"))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:  # pragma: no cover - reported to the parent
+        queue.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("length,hq,hkv", [(8192, 32, 8), (4096 + 384, 16, 4)])
+def test_head_parallel_two_gpus_matches_single_gpu(length, hq, hkv):
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, length, hq, hkv, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():  # pragma: no cover
+            p.kill()
+    assert results[1] == "ok", results[1]
+    assert results[0] == "maxdiff 0.0", results[0]
