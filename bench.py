@@ -376,12 +376,30 @@ def c4_prefill(args) -> int:
                    "last_token_logit_cosine_vs_dense": round(cos, 5)},
         "clocks": clocks.summary(),
     }
-    print(json.dumps(line), flush=True)
+    emit_json(line)
     return 0
 
 
+_JSON_FD: int | None = None
+
+
+def emit_json(line: dict) -> None:
+    """Write the result line to the real stdout (everything else the process or its
+    libraries print goes to stderr, so stdout carries exactly one JSON line)."""
+    data = (json.dumps(line) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, data)
+
+
 def main(argv=None) -> int:
+    global _JSON_FD
     args = parse_args(argv)
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)   # library banners (NCCL, symmetric memory) go to stderr
     if args.config == "c4":
         return c4_prefill(args)
     length, Hq, Hkv, D, dtype, alpha = CONFIGS[args.config]
@@ -411,8 +429,20 @@ def main(argv=None) -> int:
     vs = v[rank * hkv_r:(rank + 1) * hkv_r].contiguous()
     qd, kd, vd = qs.to(dev)[None], ks.to(dev)[None], vs.to(dev)[None]
     out_full = torch.empty((world, hkv_r * G, length, D), dtype=dtype, device=dev) if world > 1 else None
+    # Multi-GPU reassembly: fused into the attention kernel (multicast stores into a
+    # symmetric-memory buffer) where the GPUs support NVLink multicast, else NCCL.
+    mc = None
+    if world > 1:
+        from fpv2.shard import _multicast_buffer
+
+        mc = _multicast_buffer((world * hkv_r * G, length, D), dtype, dev, None)
+    mc_args = (mc[2], rank * hkv_r * G, world * hkv_r * G) if mc else None
 
     def step():
+        if mc is not None:
+            from fpv2.shard import head_parallel_sdpa
+
+            return head_parallel_sdpa(qd, kd, vd, scale=scale, config=base_cfg, fused=True)
         out = fpv2.fpv2_sdpa(qd, kd, vd, scale=scale, config=base_cfg)
         if world > 1:
             import torch.distributed as dist
@@ -451,14 +481,18 @@ def main(argv=None) -> int:
     from fpv2.kernel import index_stage, sparse_attention
 
     def step_timed(e):
+        if mc is not None:
+            mc[1].barrier(channel=0)   # no rank still reads the previous output
         e[0].record(stream)
         pk_, pv_, lists_, _ = index_stage(qd[0], kd[0], vd[0], scale=scale, config=cfg, offset=0,
                                           query_length=length, key_length=length)
         e[1].record(stream)
         out = sparse_attention(qd[0], kd[0], vd[0], pk_, pv_, *lists_, scale=scale, config=cfg,
-                               offset=0, query_length=length, key_length=length)
+                               offset=0, query_length=length, key_length=length, multicast=mc_args)
         e[2].record(stream)
-        if world > 1:
+        if mc is not None:
+            mc[1].barrier(channel=0)   # every rank's output tiles have landed everywhere
+        elif world > 1:
             import torch.distributed as dist
 
             dist.all_gather_into_tensor(out_full.view(-1), out.view(-1))
@@ -582,13 +616,17 @@ def main(argv=None) -> int:
                             f"alpha={alpha}, correction={'on' if cfg.mean_correction else 'off'}, "
                             f"sink_tokens={cfg.sink_tokens}, window_tokens={cfg.window_tokens}, "
                             f"last_n_blocks={cfg.last_n_blocks}, tile_q={cfg.tile_q} (128 packed rows)",
-                "parallelism": f"head-parallel x{world} (+NCCL all-gather of the output)" if world > 1
+                "parallelism": (f"head-parallel x{world}, output reassembled by NVLink multicast "
+                                "stores from the attention kernel" if mc is not None else
+                                f"head-parallel x{world} (+NCCL all-gather of the output)") if world > 1
                                else "single GPU",
                 "l2": "inputs (Q+K+V) larger than the 126 MB L2 at every step",
                 "ms_per_layer": round(ms_per_step, 4),
                 "index_stage_ms": round(idx_ms, 4),
                 "attention_ms": round(attn_ms, 4),
                 "allgather_ms": round(gather_ms, 4) if world > 1 else 0.0,
+                "reassembly": ("multicast stores in the attention kernel" if mc is not None
+                               else "NCCL all-gather") if world > 1 else "none",
                 "retained_tflop_per_layer": round(flops_layer / 1e12, 4),
                 "dense_causal_tflop_per_layer": round(dense_flops / 1e12, 3),
                 "block_sparsity": round(sparsity, 4),
@@ -617,7 +655,7 @@ def main(argv=None) -> int:
             "gpu_launches": 3 * args.steps,
             "clocks": clocks.summary(),
         }
-        print(json.dumps(line), flush=True)
+        emit_json(line)
     if world > 1:
         import torch.distributed as dist
 
@@ -656,7 +694,7 @@ def reference_arm(args, length, Hq, Hkv, D, dtype, cfg) -> int:
         "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit_json(line)
     return 0
 
 

@@ -117,7 +117,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap tmap_k,
                    const __grid_constant__ CUtensorMap tmap_v,
                    const __grid_constant__ CUtensorMap tmap_pk,
-                   const __grid_constant__ CUtensorMap tmap_pv, Params p) {
+                   const __grid_constant__ CUtensorMap tmap_pv,
+                   const __grid_constant__ CUtensorMap tmap_o, Params p) {
   using C = Cfg<D>;
   const AttnArgs& a = p.a;
   extern __shared__ uint8_t smem_raw[];
@@ -150,7 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* o_free = o_full + 1;         // [1]
   uint64_t* drain = o_free + 1;          // [1]
   uint64_t* lbar = drain + 1;            // [4] epilogue (m_h, l_h) exchange of a warp pair
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(lbar + 4);
+  uint64_t* obar = lbar + 4;             // [2] output tile staged (per 64-column box)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(obar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -159,7 +161,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&q_full[i]), 1);
-      mbar_init(smem_u32(&q_empty[i]), 1);
+      // last QK + the output stores (two tensor stores, or eight warps' multicast stores)
+      mbar_init(smem_u32(&q_empty[i]), 1 + (a.out_mc != nullptr ? 8 : 2));
     }
     for (int i = 0; i < kRecs; ++i) {
       mbar_init(smem_u32(&rec_full[i]), 1);
@@ -180,6 +183,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(smem_u32(o_free), 8);
     mbar_init(smem_u32(drain), 1);
     for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&lbar[i]), 2);
+    mbar_init(smem_u32(&obar[0]), D == 128 ? 4 : 8);
+    mbar_init(smem_u32(&obar[1]), 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -542,6 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool row_valid = false;
     float m_used = kFiniteMin, l = 0.f;   // this half's running max and sum
     int pv_wi = 0;
+    bool stored = false;                  // this thread issued output tensor stores
     while (ok) {
       const int ri = icount % kRecs;
       ok = mbar_wait(smem_u32(&rec_full[ri]), (icount / kRecs) & 1, wc);
@@ -706,10 +712,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        using T = typename Elem<DT>::T;
-        // this warp writes output columns [half * D/2, half * D/2 + D/2)
-        T* out = reinterpret_cast<T*>(a.out) +
-                 (((long long)(ck.h * a.G + gq)) * a.Lq_pad + row) * D + half * (D / 2);
+        // The output tile is staged in this item's Q buffer (its last QK has
+        // completed) in the TMA box layout -- rows of 64 columns, 128-byte
+        // swizzle -- and written with one coalesced tensor store per 64-column
+        // half; the buffer is released to the producer once the store has read it.
+        const int qs = wi & 1;
+        const uint32_t stage = q_smem + qs * C::kTileBytes;
         const uint32_t o0 = tmem_base + lane_off + C::kOCol + half * (D / 2);
 #pragma unroll 1
         for (int dc = 0; dc < D / 64; ++dc) {
@@ -732,16 +740,79 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __uint_as_float(x0[2 * j + 1]) * w_lo + __uint_as_float(x1[2 * j + 1]) * w_hi;
             packed[j] = pack2<DT>(v0, v1);
           }
-          uint4* dst = reinterpret_cast<uint4*>(out + dc * 32);
+          const int col0 = half * (D / 2) + dc * 32;   // first output column of these 32
+          const uint32_t rowb = stage + (col0 / 64) * 16384 + r * 128;
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+          for (int j = 0; j < 4; ++j) {
+            const int chunk = ((col0 % 64) >> 3) + j;
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rowb + ((chunk ^ (r & 7)) << 4)),
+                         "r"(packed[4 * j]), "r"(packed[4 * j + 1]), "r"(packed[4 * j + 2]),
+                         "r"(packed[4 * j + 3])
+                         : "memory");
+          }
+        }
+        fence_proxy_async_smem();
+        // D = 128: each half owns one 64-column box (its 4 warps arrive);
+        // D = 64: both halves share the box (all 8 warps arrive, half 0 stores).
+        const int ob = D == 128 ? half : 0;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&obar[ob]));
+        bool good = true;
+        if (a.out_mc != nullptr) {
+          // Multicast output: every thread of the box's warps copies 16-byte
+          // chunks of the staged box (consecutive threads along a row) to the
+          // same place of every rank's full output through the NVLink switch.
+          good = mbar_wait(smem_u32(&obar[ob]), wi & 1, wc);
+          good = __all_sync(0xffffffffu, good);
+          if (good) {
+            constexpr int kThr = D == 128 ? 128 : 256;
+            const int tid = (D == 128 ? 0 : half * 128) + quarter * 32 + lane;
+            const int P0 = ck.c * 128;
+            for (int kc = tid; kc < 1024; kc += kThr) {
+              const int rr = kc >> 3, cc = kc & 7;
+              uint4 v;
+              asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                           : "r"(stage + ob * 16384 + rr * 128 + ((cc ^ (rr & 7)) << 4)));
+              const int P = P0 + rr;
+              const long long head = a.mc_head_offset + ck.h * a.G + P / a.tile_q;
+              const long long pos = (long long)ck.t * a.tile_q + P % a.tile_q;
+              char* dst = reinterpret_cast<char*>(a.out_mc) +
+                          ((head * a.Lq_pad + pos) * D + ob * 64 + cc * 8) * 2;
+              multimem_st16(dst, v);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&q_empty[qs]));
+            stored = true;
+          }
+        } else if (quarter == 0 && lane == 0) {
+          if (D == 128 || half == 0) {
+            good = mbar_wait(smem_u32(&obar[ob]), wi & 1, wc);
+            if (good) {
+              const int P0 = ck.c * 128;
+              tma_store_3d(&tmap_o, stage + ob * 16384, ob * 64, ck.t * a.tile_q + P0 % a.tile_q,
+                           ck.h * a.G + P0 / a.tile_q);
+              bulk_commit();
+              bulk_wait_read();
+              stored = true;
+            }
+          }
+          if (good) mbar_arrive(smem_u32(&q_empty[qs]));
+        }
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) {
+          ok = false;
+          break;
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(o_free));
         ++wi;
       }
+    }
+    if (stored) {   // output stores complete (and visible to the other GPUs) before the CTA retires
+      if (a.out_mc != nullptr) asm volatile("fence.acq_rel.sys;" ::: "memory");
+      else bulk_wait_all();
     }
   }
 
@@ -754,7 +825,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int D>
 size_t smem_bytes() {
   return 1024 + (size_t)(2 + 2 * kStages) * Cfg<D>::kTileBytes + sizeof(Rec) * kRecs +
-         4 * kMaskWordsMax + 4 * (4 * 128 + 4 * 128) + 8 * (4 + 2 * kRecs + 8 * kStages + 8) + 16;
+         4 * kMaskWordsMax + 4 * (4 * 128 + 4 * 128) + 8 * (4 + 2 * kRecs + 8 * kStages + 10) + 16;
 }
 
 }  // namespace
@@ -787,8 +858,12 @@ cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, int* sched, cud
 
   const int box_rows = a.tile_q >= 128 ? 128 : a.tile_q;
   const int box_heads = 128 / box_rows;
-  CUtensorMap tq, tk, tv, tpk, tpv;
+  CUtensorMap tq, tk, tv, tpk, tpv, to;
   if (!encode_tmap_3d(&tq, a.q, a.dt, a.D, a.Lq_pad, a.Hq, 64, box_rows, box_heads))
+    return cudaErrorInvalidValue;
+  // (with a multicast output the local tensor map is unused; q stands in for it)
+  if (!encode_tmap_3d(&to, a.out_mc != nullptr ? a.q : a.out, a.dt, a.D, a.Lq_pad, a.Hq, 64,
+                      box_rows, box_heads))
     return cudaErrorInvalidValue;
   if (!encode_tmap_3d(&tk, a.k, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return cudaErrorInvalidValue;
   if (!encode_tmap_3d(&tv, a.v, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return cudaErrorInvalidValue;
@@ -812,7 +887,7 @@ cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, int* sched, cud
     e = cudaFuncSetAttribute(attn_tc_kernel<DD, TT>,                                        \
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
     if (e != cudaSuccess) return e;                                                         \
-    attn_tc_kernel<DD, TT><<<grid, kThreads, smem, stream>>>(tq, tk, tv, tpk, tpv, p);      \
+    attn_tc_kernel<DD, TT><<<grid, kThreads, smem, stream>>>(tq, tk, tv, tpk, tpv, to, p);  \
   }
   if (a.D == 64 && a.dt == DT_BF16) FPV2_ATTN_LAUNCH(64, DT_BF16)
   else if (a.D == 64 && a.dt == DT_F16) FPV2_ATTN_LAUNCH(64, DT_F16)

@@ -396,16 +396,20 @@ int fpv2_index_stage(const void* q, const void* k, const void* v, int dtype,
   return run_select(g, q, dtype, pooled_k, pooled_dtype, selected, lists, *d, s);
 }
 
-int fpv2_sparse_attention(const void* q, const void* k, const void* v, const void* pooled_k,
-                          const void* pooled_v, int pooled_dtype,
-                          const int32_t* selected_ids, const int32_t* selected_counts,
-                          const int32_t* pruned_ids, const int32_t* pruned_counts, int dtype,
-                          int32_t q_heads, int32_t kv_heads, int32_t padded_q_len,
-                          int32_t padded_k_len, int32_t head_dim, int32_t offset,
-                          int32_t query_length, int32_t key_length, float scale,
-                          int32_t block_k, int32_t tile_q, int32_t mean_correction,
-                          void* out, void* workspace, int64_t workspace_bytes,
-                          void* stream) {
+namespace fpv2 {
+namespace {
+
+// Shared body of fpv2_sparse_attention and fpv2_sparse_attention_multicast.
+int run_sparse_attention(const void* q, const void* k, const void* v, const void* pooled_k,
+                         const void* pooled_v, int pooled_dtype, const int32_t* selected_ids,
+                         const int32_t* selected_counts, const int32_t* pruned_ids,
+                         const int32_t* pruned_counts, int dtype, int32_t q_heads,
+                         int32_t kv_heads, int32_t padded_q_len, int32_t padded_k_len,
+                         int32_t head_dim, int32_t offset, int32_t query_length,
+                         int32_t key_length, float scale, int32_t block_k, int32_t tile_q,
+                         int32_t mean_correction, void* out, void* out_mc, int32_t head_offset,
+                         int32_t heads_total, void* workspace, int64_t workspace_bytes,
+                         void* stream) {
   if (dtype != DT_F16 && dtype != DT_BF16)
     return fail(FPV2_ERR_INVALID_ARGUMENT, "q, k, and v must share float16 or bfloat16 dtype");
   if (pooled_dtype != dtype && pooled_dtype != DT_F32)
@@ -423,9 +427,12 @@ int fpv2_sparse_attention(const void* q, const void* k, const void* v, const voi
     return fail(FPV2_ERR_INVALID_ARGUMENT, "key_length must fit within padded k/v");
   if (offset < 0 || (long long)offset + query_length > key_length)
     return fail(FPV2_ERR_INVALID_ARGUMENT, "offset does not align queries within the key sequence");
-  if (!q || !k || !v || !out || !selected_ids || !selected_counts ||
+  if (!q || !k || !v || (!out && !out_mc) || !selected_ids || !selected_counts ||
       (mean_correction && (!pooled_k || !pooled_v || !pruned_ids || !pruned_counts)))
     return fail(FPV2_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (out_mc != nullptr &&
+      (head_offset < 0 || heads_total < q_heads || head_offset > heads_total - q_heads))
+    return fail(FPV2_ERR_INVALID_ARGUMENT, "multicast output heads out of range");
   DeviceInfo* d = nullptr;
   int rc = device_info(&d);
   if (rc != FPV2_OK) return rc;
@@ -458,11 +465,15 @@ int fpv2_sparse_attention(const void* q, const void* k, const void* v, const voi
   a.corr = mean_correction ? 1 : 0;
   a.scale_log2 = scale * kLog2e;
   a.corr_shift = (float)log2((double)block_k);
+  a.out_mc = out_mc;
+  a.mc_head_offset = head_offset;
+  a.mc_heads = heads_total;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool aligned = reinterpret_cast<uintptr_t>(q) % 16 == 0 &&
                        reinterpret_cast<uintptr_t>(k) % 16 == 0 &&
                        reinterpret_cast<uintptr_t>(v) % 16 == 0 &&
                        reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(out_mc) % 16 == 0 &&
                        (!a.corr || (reinterpret_cast<uintptr_t>(pooled_k) % 16 == 0 &&
                                     reinterpret_cast<uintptr_t>(pooled_v) % 16 == 0));
   cudaError_t e;
@@ -472,11 +483,52 @@ int fpv2_sparse_attention(const void* q, const void* k, const void* v, const voi
                      : nullptr;
     e = launch_attn_tc(a, tc_launch(*d), sched, s);
     if (e != cudaSuccess) return cuda_fail(e, "attn_tc launch");
+  } else if (out_mc != nullptr) {
+    return fail(FPV2_ERR_UNSUPPORTED,
+                "multicast output needs the tcgen05 path (bf16/fp16, head_dim 64/128, aligned)");
   } else {
     e = launch_attn_generic(a, s);
     if (e != cudaSuccess) return cuda_fail(e, "attn_generic launch");
   }
   return FPV2_OK;
+}
+
+}  // namespace
+}  // namespace fpv2
+
+int fpv2_sparse_attention(const void* q, const void* k, const void* v, const void* pooled_k,
+                          const void* pooled_v, int pooled_dtype,
+                          const int32_t* selected_ids, const int32_t* selected_counts,
+                          const int32_t* pruned_ids, const int32_t* pruned_counts, int dtype,
+                          int32_t q_heads, int32_t kv_heads, int32_t padded_q_len,
+                          int32_t padded_k_len, int32_t head_dim, int32_t offset,
+                          int32_t query_length, int32_t key_length, float scale,
+                          int32_t block_k, int32_t tile_q, int32_t mean_correction,
+                          void* out, void* workspace, int64_t workspace_bytes,
+                          void* stream) {
+  return fpv2::run_sparse_attention(q, k, v, pooled_k, pooled_v, pooled_dtype, selected_ids,
+                                    selected_counts, pruned_ids, pruned_counts, dtype, q_heads,
+                                    kv_heads, padded_q_len, padded_k_len, head_dim, offset,
+                                    query_length, key_length, scale, block_k, tile_q,
+                                    mean_correction, out, nullptr, 0, 0, workspace,
+                                    workspace_bytes, stream);
+}
+
+int fpv2_sparse_attention_multicast(
+    const void* q, const void* k, const void* v, const void* pooled_k, const void* pooled_v,
+    int pooled_dtype, const int32_t* selected_ids, const int32_t* selected_counts,
+    const int32_t* pruned_ids, const int32_t* pruned_counts, int dtype, int32_t q_heads,
+    int32_t kv_heads, int32_t padded_q_len, int32_t padded_k_len, int32_t head_dim,
+    int32_t offset, int32_t query_length, int32_t key_length, float scale, int32_t block_k,
+    int32_t tile_q, int32_t mean_correction, void* out_multicast, int32_t head_offset,
+    int32_t heads_total, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (out_multicast == nullptr) return fail(FPV2_ERR_INVALID_ARGUMENT, "null multicast output");
+  return fpv2::run_sparse_attention(q, k, v, pooled_k, pooled_v, pooled_dtype, selected_ids,
+                                    selected_counts, pruned_ids, pruned_counts, dtype, q_heads,
+                                    kv_heads, padded_q_len, padded_k_len, head_dim, offset,
+                                    query_length, key_length, scale, block_k, tile_q,
+                                    mean_correction, nullptr, out_multicast, head_offset,
+                                    heads_total, workspace, workspace_bytes, stream);
 }
 
 int fpv2_fast_path_mask(int dtype, int32_t q_heads, int32_t kv_heads, int32_t head_dim,

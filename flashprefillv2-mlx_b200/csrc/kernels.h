@@ -64,6 +64,12 @@ struct AttnArgs {
   int offset, valid_lq, valid_lk, block_k, tile_q, corr;
   float scale_log2;   // scale * log2(e)
   float corr_shift;   // log2(block_k)
+  // Optional multicast output: the NVLink multicast address of a full
+  // [mc_heads, Lq_pad, D] output shared by every rank; this call's query head
+  // hq lands at head mc_head_offset + hq. Null: write `out` only.
+  void* out_mc = nullptr;
+  int mc_head_offset = 0;
+  int mc_heads = 0;
 };
 cudaError_t launch_attn_generic(const AttnArgs& a, cudaStream_t stream);
 

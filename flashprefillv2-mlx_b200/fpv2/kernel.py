@@ -153,7 +153,8 @@ def sparse_attention(
     key_length: int | None = None,
     tile: TileConfig | None = None,
     pack_gqa: bool = False,
-) -> torch.Tensor:
+    multicast: tuple[int, int, int] | None = None,
+) -> torch.Tensor | None:
     """Tiled block-sparse attention with the pooled mean correction.
 
     Validation and error messages follow fpv2/kernel.py:465-510. Pooled K/V may
@@ -161,6 +162,11 @@ def sparse_attention(
     (fpv2/kernel.py:553-554). Ids are clipped to the block range
     (fpv2/kernel.py:555-558). Rows at or beyond ``query_length`` are padding and
     their output is unspecified.
+
+    ``multicast=(address, head_offset, heads_total)`` (not in the reference: the
+    head-parallel multi-GPU layer) writes the output into every rank's full
+    ``[heads_total, padded_q_len, dim]`` buffer behind an NVLink multicast
+    address instead of a new tensor, at head ``head_offset + h``, and returns None.
     """
     if q.ndim != 3 or k.ndim != 3 or v.ndim != 3:
         raise ValueError("q, k, and v must have shape [heads, sequence, dim]")
@@ -214,15 +220,23 @@ def sparse_attention(
     qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
     pkc, pvc = pooled_k.contiguous(), pooled_v.contiguous()
     lc = [x.contiguous() for x in (selected_ids, selected_counts, pruned_ids, pruned_counts)]
-    out = torch.empty_like(qc)
     workspace = torch.empty(_lib.ATTN_WORKSPACE_BYTES // 4, dtype=torch.int32, device=q.device)
-    _lib.check(_lib.lib().fpv2_sparse_attention(
+    args = (
         _lib.ptr(qc), _lib.ptr(kc), _lib.ptr(vc), _lib.ptr(pkc), _lib.ptr(pvc),
         _lib.dtype_code(pkc.dtype), _lib.ptr(lc[0]), _lib.ptr(lc[1]), _lib.ptr(lc[2]),
         _lib.ptr(lc[3]), _lib.dtype_code(q.dtype), query_heads, kv_heads, padded_query_length,
         padded_key_length, head_dim, offset, valid_query_length, valid_key_length, float(scale),
-        config.block_k, config.tile_q, 1 if config.mean_correction else 0, _lib.ptr(out),
-        _lib.ptr(workspace), workspace.numel() * 4, _lib.stream_of(q)))
+        config.block_k, config.tile_q, 1 if config.mean_correction else 0,
+    )
+    if multicast is not None:
+        mc_ptr, head_offset, heads_total = multicast
+        _lib.check(_lib.lib().fpv2_sparse_attention_multicast(
+            *args, mc_ptr, head_offset, heads_total, _lib.ptr(workspace), workspace.numel() * 4,
+            _lib.stream_of(q)))
+        return None
+    out = torch.empty_like(qc)
+    _lib.check(_lib.lib().fpv2_sparse_attention(
+        *args, _lib.ptr(out), _lib.ptr(workspace), workspace.numel() * 4, _lib.stream_of(q)))
     return out
 
 

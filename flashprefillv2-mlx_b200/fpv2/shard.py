@@ -72,6 +72,33 @@ def gather_heads(local: torch.Tensor, group=None, out: torch.Tensor | None = Non
     return out.permute(1, 0, 2, 3, 4).reshape(b, world * h, l, d)
 
 
+_SYMM_BUFFERS: dict = {}
+
+
+def _multicast_buffer(shape, dtype, device, group):
+    """Full-output buffer in torch symmetric memory, bound to an NVLink multicast
+    object across the group (cached per shape). Returns (tensor, handle,
+    multicast address of the tensor) or None when the GPUs offer no multicast."""
+    key = (tuple(shape), dtype, device, id(group))
+    if key in _SYMM_BUFFERS:
+        return _SYMM_BUFFERS[key]
+    import torch.distributed._symmetric_memory as symm_mem
+
+    grp = group if group is not None else dist.group.WORLD
+    buf = symm_mem.empty(*shape, dtype=dtype, device=device)
+    handle = symm_mem.rendezvous(buf, grp)
+    entry = None
+    mc_base = int(getattr(handle, "multicast_ptr", 0) or 0)
+    if mc_base:
+        # the tensor's offset inside the symmetric allocation is the same in the
+        # local mapping and in the multicast mapping
+        off = buf.data_ptr() - int(handle.buffer_ptrs[handle.rank])
+        if 0 <= off and off + buf.numel() * buf.element_size() <= int(handle.buffer_size):
+            entry = (buf, handle, mc_base + off)
+    _SYMM_BUFFERS[key] = entry
+    return entry
+
+
 def head_parallel_sdpa(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -80,11 +107,40 @@ def head_parallel_sdpa(
     scale: float,
     config: FPV2Config = FPV2Config(),
     group=None,
+    fused: bool | None = None,
 ) -> torch.Tensor:
-    """FPV2 on this rank's head shard (``[1, Hq/P, L, D]``, ``[1, Hkv/P, L, D]``), then
-    one all-gather: every rank returns the full ``[1, Hq, L, D]`` output."""
-    local = fpv2_sdpa(q, k, v, scale=scale, config=config)
-    return gather_heads(local, group)
+    """FPV2 on this rank's head shard (``[1, Hq/P, L, D]``, ``[1, Hkv/P, L, D]``);
+    every rank returns the full ``[1, Hq, L, D]`` output.
+
+    Fused (the default where the GPUs support NVLink multicast): the attention
+    kernel writes each finished output tile straight into every rank's copy of
+    the full output through the multicast address (torch symmetric memory), so
+    the reassembly overlaps the computation; the returned tensor is a view of
+    that shared buffer, valid until the next call with the same shape. Otherwise
+    one NCCL all-gather follows the kernel."""
+    from fpv2 import _lib
+    from fpv2.patch import _effective_config
+
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    hq, lq, d = q.shape[1], q.shape[2], q.shape[3]
+    eff = _effective_config(config, hq, k.shape[1])
+    if fused is None:
+        fused = (world > 1 and eff is not None and q.is_cuda
+                 and dist.get_backend(group) == "nccl"
+                 and _lib.fast_path_mask(q.dtype, hq, k.shape[1], d, eff.block_k, eff.tile_q, 1) & 2)
+    entry = None
+    if fused:
+        lq_pad = (lq + eff.tile_q - 1) // eff.tile_q * eff.tile_q
+        entry = _multicast_buffer((world * hq, lq_pad, d), q.dtype, q.device, group)
+    if entry is None:
+        local = fpv2_sdpa(q, k, v, scale=scale, config=config)
+        return gather_heads(local, group)
+    buf, handle, mc_addr = entry
+    rank = dist.get_rank(group)
+    handle.barrier(channel=0)   # no rank still reads the previous contents
+    fpv2_sdpa(q, k, v, scale=scale, config=config, multicast=(mc_addr, rank * hq, world * hq))
+    handle.barrier(channel=0)   # every rank's tiles have landed in every buffer
+    return buf[None, :, :lq, :]
 
 
 class RankMonitor:

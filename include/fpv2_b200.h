@@ -156,6 +156,28 @@ FPV2_API int fpv2_sparse_attention(const void* q, const void* k, const void* v, 
                           void* stream);
 
 /*
+ * fpv2_sparse_attention for the head-parallel multi-GPU layer, with the output
+ * all-gather fused into the kernel (no counterpart in the reference, which runs
+ * on one device; it replaces the NCCL all-gather that reassembles the layer
+ * output). `out_multicast` is the NVLink multicast address of a full output
+ * [heads_total, padded_q_len, head_dim] buffer bound on every rank (for
+ * example torch symmetric memory); this call's query head hq is written to
+ * head `head_offset + hq` of every rank's buffer as each output tile
+ * completes, with 16-byte multimem stores. Needs the tcgen05 path (bf16/fp16,
+ * head_dim 64 or 128, 16-byte aligned pointers), else FPV2_ERR_UNSUPPORTED.
+ * The caller orders the ranks around the call (a cross-rank barrier after it
+ * before reading the buffer, and before reusing it).
+ */
+FPV2_API int fpv2_sparse_attention_multicast(
+    const void* q, const void* k, const void* v, const void* pooled_k, const void* pooled_v,
+    int pooled_dtype, const int32_t* selected_ids, const int32_t* selected_counts,
+    const int32_t* pruned_ids, const int32_t* pruned_counts, int dtype, int32_t q_heads,
+    int32_t kv_heads, int32_t padded_q_len, int32_t padded_k_len, int32_t head_dim,
+    int32_t offset, int32_t query_length, int32_t key_length, float scale, int32_t block_k,
+    int32_t tile_q, int32_t mean_correction, void* out_multicast, int32_t head_offset,
+    int32_t heads_total, void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * fpv2_sparse_attention for callers that cannot allocate device memory (no
  * counterpart in the reference). Same arguments and results as
  * fpv2_sparse_attention without the workspace: the kernel's work-queue counter

@@ -1,7 +1,10 @@
-"""Head-parallel FPV2 on two GPUs (NCCL) equals the single-GPU layer.
+"""Head-parallel FPV2 on two GPUs equals the single-GPU layer.
 
 Each rank runs the index stage and the sparse attention on its KV-head shard
-(and the matching query heads); one NCCL all-gather reassembles the output.
+(and the matching query heads). The output is reassembled either by the
+attention kernel itself (multicast stores into a symmetric-memory buffer, where
+the GPUs support NVLink multicast) or by one NCCL all-gather; both must equal
+the single-GPU layer on every rank.
 Every selection reduction, list and K/V read of the path belongs to one KV
 head, so the sharded layer must reproduce the single-GPU layer bit for bit.
 Skipped unless at least two GPUs are visible.
@@ -50,16 +53,18 @@ def _worker(rank: int, world: int, port: int, length: int, hq: int, hkv: int, qu
         q, k, v = _inputs(length, hq, hkv)
         sh = head_shard(hq, hkv, world, rank)
         ql, kl, vl = (t.to(dev) for t in shard_inputs(q, k, v, sh))
+        from fpv2.shard import _SYMM_BUFFERS
+
         cfg = fpv2.FPV2Config(alpha=0.1)
-        out = head_parallel_sdpa(ql, kl, vl, scale=128 ** -0.5, config=cfg)
-        torch.cuda.synchronize(dev)
-        if rank == 0:
-            ref = fpv2.fpv2_sdpa(q.to(dev), k.to(dev), v.to(dev), scale=128 ** -0.5, config=cfg)
+        ref = fpv2.fpv2_sdpa(q.to(dev), k.to(dev), v.to(dev), scale=128 ** -0.5, config=cfg)
+        report = []
+        for fused in (False, True, True):   # NCCL, then the fused path twice (buffer reuse)
+            out = head_parallel_sdpa(ql, kl, vl, scale=128 ** -0.5, config=cfg, fused=fused)
             torch.cuda.synchronize(dev)
             diff = (out.float() - ref.float()).abs().max().item()
-            queue.put((rank, f"maxdiff {diff}"))
-        else:
-            queue.put((rank, "ok"))
+            report.append(f"{diff}")
+        multicast = any(e is not None for e in _SYMM_BUFFERS.values())
+        queue.put((rank, f"maxdiff {' '.join(report)} multicast {multicast}"))
         dist.barrier()
         dist.destroy_process_group()
     except Exception:  # pragma: no cover - reported to the parent
@@ -80,5 +85,5 @@ def test_head_parallel_two_gpus_matches_single_gpu(length, hq, hkv):
         p.join(timeout=120)
         if p.is_alive():  # pragma: no cover
             p.kill()
-    assert results[1] == "ok", results[1]
-    assert results[0] == "maxdiff 0.0", results[0]
+    for rank in (0, 1):
+        assert results[rank].startswith("maxdiff 0.0 0.0 0.0 multicast"), results[rank]
