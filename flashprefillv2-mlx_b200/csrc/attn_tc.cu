@@ -21,7 +21,10 @@
 // m = max(m_0, m_1), which equals the single online softmax over all keys.
 // So the two warps that share a row never exchange anything per KV item.
 // Each running max is rescaled lazily: O_h is only rescaled when m_h grows by
-// more than 2^8, which leaves the final result unchanged.
+// more than a factor 2^16 (2^15 for fp16), which leaves the final result
+// unchanged. The softmax arithmetic runs on packed fp32 pairs (one FMA and one
+// add per two keys) and three-input maxima, which leaves the MUFU exponentials
+// as the only per-key scalar work.
 //
 // Pooled correction: instead of gathering the pruned blocks' pooled rows, the
 // producer streams contiguous 128-row tiles of the head's pooled K/V with TMA
@@ -612,30 +615,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             vm1 = nv1 >= 32 ? 0xffffffffu : (nv1 <= 0 ? 0u : ((1u << nv1) - 1u));
           }
         }
-        // x = s * c2 + bias in the log2 domain; a masked entry takes finite_min,
-        // exactly as the reference kernel masks its logits. One exp loop serves
-        // every kind of item; only partially valid warps pay for the selects.
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          s[0][j] = __float_as_uint(fmaf(__uint_as_float(s[0][j]), c2, bias));
-          s[1][j] = __float_as_uint(fmaf(__uint_as_float(s[1][j]), c2, bias));
-        }
+        // Full warps keep the raw scores (c2 > 0 keeps the order; x = s*c2 + bias
+        // is formed inside the exponent); a warp with any invalid entry forms
+        // x = s*c2 + bias and gives masked entries finite_min, exactly as the
+        // reference kernel masks its logits.
+        float mt;
         if (!full) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            s[0][j] = ((vm0 >> j) & 1u) ? s[0][j] : __float_as_uint(kFiniteMin);
-            s[1][j] = ((vm1 >> j) & 1u) ? s[1][j] : __float_as_uint(kFiniteMin);
+            const float x0 = fmaf(__uint_as_float(s[0][j]), c2, bias);
+            const float x1 = fmaf(__uint_as_float(s[1][j]), c2, bias);
+            s[0][j] = ((vm0 >> j) & 1u) ? __float_as_uint(x0) : __float_as_uint(kFiniteMin);
+            s[1][j] = ((vm1 >> j) & 1u) ? __float_as_uint(x1) : __float_as_uint(kFiniteMin);
           }
         }
-        float mx0 = kFiniteMin, mx1 = kFiniteMin, mx2 = kFiniteMin, mx3 = kFiniteMin;
+        {
+          float mx0 = max3f(__uint_as_float(s[0][0]), __uint_as_float(s[0][1]), __uint_as_float(s[0][2]));
+          float mx1 = max3f(__uint_as_float(s[0][16]), __uint_as_float(s[0][17]), __uint_as_float(s[0][18]));
+          float mx2 = max3f(__uint_as_float(s[1][0]), __uint_as_float(s[1][1]), __uint_as_float(s[1][2]));
+          float mx3 = max3f(__uint_as_float(s[1][16]), __uint_as_float(s[1][17]), __uint_as_float(s[1][18]));
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          mx0 = fmaxf(mx0, __uint_as_float(s[0][j]));
-          mx1 = fmaxf(mx1, __uint_as_float(s[0][j + 1]));
-          mx2 = fmaxf(mx2, __uint_as_float(s[1][j]));
-          mx3 = fmaxf(mx3, __uint_as_float(s[1][j + 1]));
+          for (int j = 3; j < 15; j += 2) {
+            mx0 = max3f(mx0, __uint_as_float(s[0][j]), __uint_as_float(s[0][j + 1]));
+            mx1 = max3f(mx1, __uint_as_float(s[0][16 + j]), __uint_as_float(s[0][17 + j]));
+            mx2 = max3f(mx2, __uint_as_float(s[1][j]), __uint_as_float(s[1][j + 1]));
+            mx3 = max3f(mx3, __uint_as_float(s[1][16 + j]), __uint_as_float(s[1][17 + j]));
+          }
+          mx0 = max3f(mx0, __uint_as_float(s[0][15]), mx1);
+          mx2 = max3f(mx2, __uint_as_float(s[1][15]), mx3);
+          const float m4 = max3f(mx0, mx2, fmaxf(__uint_as_float(s[0][31]), __uint_as_float(s[1][31])));
+          mt = full ? fmaf(m4, c2, bias) : m4;
         }
-        const float mt = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
         const float m_new = fmaxf(m_used, mt);
         const bool need = m_new > m_used + RescaleT<DT>::value ||
                           (m_used == kFiniteMin && m_new > kFiniteMin);
@@ -666,22 +676,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // P = 2^(x - m): a masked entry (x = finite_min) weighs 1 while the half
         // has seen nothing but masked entries (m = finite_min), else 0.
-        float rs0 = 0.f, rs1 = 0.f, rs2 = 0.f, rs3 = 0.f;
+        // x - m = fma(s, c2, bias - m) for a full warp, fma(x, 1, -m) otherwise (exact);
+        // pairs of keys share one packed FMA and one packed add of the row sums.
+        const float2 cm2 = full ? make_float2(c2, c2) : make_float2(1.f, 1.f);
+        const float2 nb2 = full ? make_float2(bias - m_used, bias - m_used) : make_float2(-m_used, -m_used);
+        float2 rs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                        make_float2(0.f, 0.f)};
         uint32_t pk[32];
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const float p0 = ex2(__uint_as_float(s[0][j]) - m_used);
-          const float p1 = ex2(__uint_as_float(s[0][j + 1]) - m_used);
-          const float p2 = ex2(__uint_as_float(s[1][j]) - m_used);
-          const float p3 = ex2(__uint_as_float(s[1][j + 1]) - m_used);
-          rs0 += p0;
-          rs1 += p1;
-          rs2 += p2;
-          rs3 += p3;
-          pk[j >> 1] = pack_p<DT>(p0, p1);
-          pk[16 + (j >> 1)] = pack_p<DT>(p2, p3);
+        for (int c = 0; c < 2; ++c) {
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const float2 xv = fma_f32x2(
+                make_float2(__uint_as_float(s[c][2 * q]), __uint_as_float(s[c][2 * q + 1])), cm2, nb2);
+            float2 pv;
+            pv.x = ex2(xv.x);
+            pv.y = ex2(xv.y);
+            rs[q & 3] = add_f32x2(rs[q & 3], pv);
+            pk[16 * c + q] = pack_p<DT>(pv.x, pv.y);
+          }
         }
-        l += (rs0 + rs1) + (rs2 + rs3);
+        l += ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
         // P_h -> the first 32 columns of this half's own S columns (already read)
         tmem_st32(s_tmem, pk);
         tmem_wait_st();
