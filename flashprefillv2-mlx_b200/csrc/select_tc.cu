@@ -368,52 +368,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                   vm[q2] = bits;
                 }
               }
-              float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
-              if (!masked) {
+              // Masked-out entries become -inf: they drop out of the max and
+              // 2^(-inf) = 0 drops them from the sum.
+              if (masked) {
 #pragma unroll
-                for (int j = 0; j < 32; j += 2) {
-                  m0 = fmaxf(m0, __uint_as_float(sv[0][j]));
-                  m1 = fmaxf(m1, __uint_as_float(sv[0][j + 1]));
-                  m2 = fmaxf(m2, __uint_as_float(sv[1][j]));
-                  m3 = fmaxf(m3, __uint_as_float(sv[1][j + 1]));
-                }
-              } else {
-#pragma unroll
-                for (int j = 0; j < 32; j += 2) {
-                  m0 = ((vm[0] >> j) & 1u) ? fmaxf(m0, __uint_as_float(sv[0][j])) : m0;
-                  m1 = ((vm[0] >> (j + 1)) & 1u) ? fmaxf(m1, __uint_as_float(sv[0][j + 1])) : m1;
-                  m2 = ((vm[1] >> j) & 1u) ? fmaxf(m2, __uint_as_float(sv[1][j])) : m2;
-                  m3 = ((vm[1] >> (j + 1)) & 1u) ? fmaxf(m3, __uint_as_float(sv[1][j + 1])) : m3;
+                for (int j = 0; j < 32; ++j) {
+                  sv[0][j] = ((vm[0] >> j) & 1u) ? sv[0][j] : 0xff800000u;
+                  sv[1][j] = ((vm[1] >> j) & 1u) ? sv[1][j] : 0xff800000u;
                 }
               }
-              const float mraw = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+              float m0 = max3f(__uint_as_float(sv[0][0]), __uint_as_float(sv[0][1]), __uint_as_float(sv[0][2]));
+              float m1 = max3f(__uint_as_float(sv[0][16]), __uint_as_float(sv[0][17]), __uint_as_float(sv[0][18]));
+              float m2 = max3f(__uint_as_float(sv[1][0]), __uint_as_float(sv[1][1]), __uint_as_float(sv[1][2]));
+              float m3 = max3f(__uint_as_float(sv[1][16]), __uint_as_float(sv[1][17]), __uint_as_float(sv[1][18]));
+#pragma unroll
+              for (int j = 3; j < 15; j += 2) {
+                m0 = max3f(m0, __uint_as_float(sv[0][j]), __uint_as_float(sv[0][j + 1]));
+                m1 = max3f(m1, __uint_as_float(sv[0][16 + j]), __uint_as_float(sv[0][17 + j]));
+                m2 = max3f(m2, __uint_as_float(sv[1][j]), __uint_as_float(sv[1][j + 1]));
+                m3 = max3f(m3, __uint_as_float(sv[1][16 + j]), __uint_as_float(sv[1][17 + j]));
+              }
+              m0 = max3f(m0, __uint_as_float(sv[0][15]), m1);
+              m2 = max3f(m2, __uint_as_float(sv[1][15]), m3);
+              const float mraw = max3f(m0, m2, fmaxf(__uint_as_float(sv[0][31]), __uint_as_float(sv[1][31])));
               const float mnew = fmaxf(mb, mraw * c);
               // all lanes take the same path below (-inf maxima give ex2(-inf) = 0)
               const float nm = mnew == -INFINITY ? 0.f : -mnew;
-              float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
-              if (!masked) {
+              // pairs of scores: one packed FMA forms both exponents, packed adds sum
+              const float2 c2 = make_float2(c, c), nm2 = make_float2(nm, nm);
+              float2 e[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                             make_float2(0.f, 0.f)};
+#pragma unroll
+              for (int h2 = 0; h2 < 2; ++h2)
 #pragma unroll
                 for (int j = 0; j < 32; j += 2) {
-                  e0 += ex2(fmaf(__uint_as_float(sv[0][j]), c, nm));
-                  e1 += ex2(fmaf(__uint_as_float(sv[0][j + 1]), c, nm));
-                  e2 += ex2(fmaf(__uint_as_float(sv[1][j]), c, nm));
-                  e3 += ex2(fmaf(__uint_as_float(sv[1][j + 1]), c, nm));
+                  const float2 xv = fma_f32x2(
+                      make_float2(__uint_as_float(sv[h2][j]), __uint_as_float(sv[h2][j + 1])), c2, nm2);
+                  e[(j >> 1) & 3] = add_f32x2(e[(j >> 1) & 3], make_float2(ex2(xv.x), ex2(xv.y)));
                 }
-              } else {
-#pragma unroll
-                for (int j = 0; j < 32; j += 2) {
-                  const float x0 = ex2(fmaf(__uint_as_float(sv[0][j]), c, nm));
-                  const float x1 = ex2(fmaf(__uint_as_float(sv[0][j + 1]), c, nm));
-                  const float x2 = ex2(fmaf(__uint_as_float(sv[1][j]), c, nm));
-                  const float x3 = ex2(fmaf(__uint_as_float(sv[1][j + 1]), c, nm));
-                  e0 += ((vm[0] >> j) & 1u) ? x0 : 0.f;
-                  e1 += ((vm[0] >> (j + 1)) & 1u) ? x1 : 0.f;
-                  e2 += ((vm[1] >> j) & 1u) ? x2 : 0.f;
-                  e3 += ((vm[1] >> (j + 1)) & 1u) ? x3 : 0.f;
-                }
-              }
+              const float esum = ((e[0].x + e[0].y) + (e[1].x + e[1].y)) + ((e[2].x + e[2].y) + (e[3].x + e[3].y));
               if (mnew != -INFINITY) {
-                eb = eb * ex2(mb - mnew) + ((e0 + e1) + (e2 + e3));
+                eb = eb * ex2(mb - mnew) + esum;
                 mb = mnew;
               }
             }
