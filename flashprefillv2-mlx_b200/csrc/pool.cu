@@ -7,10 +7,16 @@
 // than ~28 binades, so the result does not depend on the summation order and
 // is reproduced bit for bit.
 //
-// HBM-streaming kernel: one CTA per (tensor, head, block); 16-byte vector
-// loads of 8 consecutive features per thread, rows spread over the CTA.
+// Streaming kernels. For 16-bit inputs whose blocks are at most 32 KB (the
+// configurations the hook runs), persistent CTAs stream whole blocks (one
+// contiguous bs x D run each) through a 3-stage shared-memory ring with
+// cp.async, so the loads of the next blocks are in flight while the current
+// block is summed; other shapes take one CTA per (tensor, head, block) with
+// 16-byte vector loads of 8 consecutive features per thread.
 #include "common.cuh"
 #include "kernels.h"
+
+#include <algorithm>
 
 namespace fpv2 {
 
@@ -95,12 +101,118 @@ __global__ void __launch_bounds__(kPoolThreads)
   }
 }
 
+
+// ---- pipelined kernel ------------------------------------------------------
+constexpr int kPipeThreads = 256;
+constexpr int kPipeStages = 3;
+constexpr int kPipeMaxUnitBytes = 32 * 1024;
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// One unit = one (tensor, head, block): `bs` consecutive rows of D features,
+// contiguous in memory. Unit u of ntensors * heads * nblk; tensor-major.
+template <int DT_IN, int DT_OUT>
+__global__ void __launch_bounds__(kPipeThreads)
+    pool_pipe_kernel(PoolArgs a, int ntensors) {
+  using Tout = typename Elem<DT_OUT>::T;
+  constexpr int kPerVec = 8;                               // 16-bit features per 16 bytes
+  extern __shared__ __align__(16) uint8_t pool_smem[];
+  const int cpr = a.D / kPerVec;                           // 16-byte chunks per row
+  const int unit_chunks = (int)a.bs * cpr;                 // multiple of kPipeThreads
+  const int unit_bytes = unit_chunks * 16;
+  const uint32_t ring = smem_u32(pool_smem);
+  double* red = reinterpret_cast<double*>(pool_smem + kPipeStages * unit_bytes);
+  const int64_t nblk = a.length / a.bs;
+  const int64_t per_tensor = a.heads * nblk;
+  const int64_t units = per_tensor * ntensors;
+  const int tid = threadIdx.x;
+  const uint8_t* const x0 = reinterpret_cast<const uint8_t*>(a.x[0]);
+  const uint8_t* const x1 = reinterpret_cast<const uint8_t*>(a.x[1]);
+  auto issue = [=](int64_t u, int stage) {
+    if (u < units) {
+      const int t = (int)(u / per_tensor);
+      const int64_t hb = u % per_tensor;                   // head * nblk + block, rows contiguous
+      const uint8_t* src = (t == 0 ? x0 : x1) + hb * (int64_t)unit_bytes;
+      const uint32_t dst = ring + stage * unit_bytes;
+      for (int q = tid; q < unit_chunks; q += kPipeThreads) cp_async16(dst + q * 16, src + q * 16);
+    }
+    cp_async_commit();   // one group per unit slot, empty past the end
+  };
+  int64_t u = blockIdx.x;
+#pragma unroll
+  for (int s = 0; s < kPipeStages - 1; ++s) issue(u + (int64_t)s * gridDim.x, s);
+  const int c = tid % cpr;                                 // this thread's 8 features
+  const int rstep = kPipeThreads / cpr;
+  for (int i = 0; u < units; ++i, u += gridDim.x) {
+    issue(u + (int64_t)(kPipeStages - 1) * gridDim.x, (i + kPipeStages - 1) % kPipeStages);
+    cp_async_wait<kPipeStages - 1>();                      // this unit's copies (own) landed
+    __syncthreads();                                       // ... and everyone else's
+    const uint8_t* st = pool_smem + (i % kPipeStages) * unit_bytes;
+    double acc[kPerVec];
+#pragma unroll
+    for (int e = 0; e < kPerVec; ++e) acc[e] = 0.0;
+    for (int r = tid / cpr; r < a.bs; r += rstep) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(st + (r * cpr + c) * 16);
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack2<DT_IN>(w[e]);
+        acc[2 * e] += (double)f.x;
+        acc[2 * e + 1] += (double)f.y;
+      }
+    }
+    const int j = tid / cpr;
+#pragma unroll
+    for (int e = 0; e < kPerVec; ++e) red[j * a.D + c * kPerVec + e] = acc[e];
+    __syncthreads();
+    for (int col = tid; col < a.D; col += kPipeThreads) {
+      double sum = 0.0;
+      for (int jj = 0; jj < rstep; ++jj) sum += red[jj * a.D + col];
+      const float m = (float)(sum / (double)a.bs);
+      const int t = (int)(u / per_tensor);
+      Tout* out = reinterpret_cast<Tout*>(t == 0 ? a.out[0] : a.out[1]);
+      out[(u % per_tensor) * a.D + col] = Elem<DT_OUT>::from_f(m);
+    }
+    __syncthreads();                                       // ring stage and red reusable
+  }
+  cp_async_wait<0>();
+}
+
 template <int DT_IN, int DT_OUT>
 cudaError_t launch_pool_t(const PoolArgs& a, int ntensors, cudaStream_t stream) {
   const int64_t nblocks = a.heads * (a.length / a.bs);
   if (nblocks == 0) return cudaSuccess;
   dim3 grid((unsigned)nblocks, (unsigned)ntensors);
   constexpr int kPerVec = 16 / (int)sizeof(typename Elem<DT_IN>::T);
+  if constexpr (kPerVec == 8) {
+   if (a.D % 8 == 0 && kPipeThreads % (a.D / 8) == 0 &&
+      (a.bs * (a.D / 8)) % kPipeThreads == 0 && a.bs * a.D * 2 <= kPipeMaxUnitBytes) {
+    bool aligned = true;
+    for (int t = 0; t < ntensors; ++t) aligned &= reinterpret_cast<uintptr_t>(a.x[t]) % 16 == 0;
+    if (aligned) {
+      int dev = 0, sms = 0;
+      cudaError_t e = cudaGetDevice(&dev);
+      if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (e != cudaSuccess) return e;
+      const int unit_bytes = (int)(a.bs * a.D * 2);
+      const size_t smem = (size_t)kPipeStages * unit_bytes +
+                          sizeof(double) * (size_t)(kPipeThreads / (a.D / 8)) * a.D;
+      e = cudaFuncSetAttribute(pool_pipe_kernel<DT_IN, DT_OUT>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      const int64_t units = nblocks * ntensors;
+      const int g = (int)std::min<int64_t>(units, 2 * (int64_t)sms);   // two CTAs per SM
+      pool_pipe_kernel<DT_IN, DT_OUT><<<g, kPipeThreads, smem, stream>>>(a, ntensors);
+      return cudaGetLastError();
+    }
+   }
+  }
   bool vec = (a.D % kPerVec == 0) && (kPoolThreads % (a.D / kPerVec) == 0);
   for (int t = 0; t < ntensors && vec; ++t)
     vec = (reinterpret_cast<uintptr_t>(a.x[t]) % 16 == 0);
