@@ -122,6 +122,27 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return r;
 }
 
+// 2^x for a pair, x <= 16, on the FMA and integer pipes instead of the MUFU:
+// n = rint(x) through the 1.5 * 2^23 rounding constant, f = x - n in
+// [-0.5, 0.5], 2^f by a quartic fitted (least maximum relative error) to
+// relative error < 2.7e-6 on that interval (checked in float32 over the whole
+// input range), and n added to the exponent field. Inputs below -126 are
+// clamped (the result is then below 2^-125).
+__device__ __forceinline__ float2 exp2_poly_x2(float2 x) {
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 t = add_f32x2(x, make_float2(12582912.f, 12582912.f));
+  const float2 n = add_f32x2(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = fma_f32x2(n, make_float2(-1.f, -1.f), x);
+  float2 p = fma_f32x2(make_float2(0.009570052f, 0.009570052f), f,
+                       make_float2(0.055917736f, 0.055917736f));
+  p = fma_f32x2(p, f, make_float2(0.24024744f, 0.24024744f));
+  p = fma_f32x2(p, f, make_float2(0.69312185f, 0.69312185f));
+  p = fma_f32x2(p, f, make_float2(0.99999928f, 0.99999928f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
 // ---------------------------------------------------------------------------
 // shared memory addressing
 // ---------------------------------------------------------------------------
