@@ -15,6 +15,7 @@ from fpv2.kernel import (
 )
 from fpv2.patch import block_sparsity, disable, enable, fpv2_sdpa, is_enabled
 from fpv2.selection import FPV2Config, block_scores_and_select, density, pool_blocks
+from fpv2.stream import sdpa_from_host
 
 __all__ = [
     "FPV2Config",
@@ -31,5 +32,6 @@ __all__ = [
     "index_stage",
     "is_enabled",
     "pool_blocks",
+    "sdpa_from_host",
     "sparse_attention",
 ]

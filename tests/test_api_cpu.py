@@ -175,3 +175,18 @@ def test_causal_bias_fall_through_is_bit_identical_on_cpu():
     finally:
         fpv2.disable()
     assert torch.equal(actual, expected)
+
+
+def test_sdpa_from_host_validates_before_touching_the_gpu():
+    import fpv2
+
+    q = torch.zeros((1, 8, 64, 128), dtype=torch.bfloat16)
+    k = torch.zeros((1, 2, 64, 128), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="host tensor"):
+        fpv2.sdpa_from_host(q.to("meta"), k, k, scale=1.0)
+    with pytest.raises(ValueError, match="kv_heads_per_chunk"):
+        fpv2.sdpa_from_host(q, k, k, scale=1.0, kv_heads_per_chunk=3)
+    with pytest.raises(ValueError, match="multiple"):
+        fpv2.sdpa_from_host(q[:, :7], k, k, scale=1.0)
+    with pytest.raises(ValueError, match="out must be"):
+        fpv2.sdpa_from_host(q, k, k, scale=1.0, out=torch.zeros((1, 8, 64, 64), dtype=torch.bfloat16))
