@@ -434,10 +434,21 @@ def main(argv=None) -> int:
     # Multi-GPU reassembly: fused into the attention kernel (multicast stores into a
     # symmetric-memory buffer) where the GPUs support NVLink multicast, else NCCL.
     mc = None
-    if world > 1:
+    if world > 1 and os.environ.get("FPV2_NO_MULTICAST", "0") != "1":
+        import torch.distributed as dist
         from fpv2.shard import _multicast_buffer
 
-        mc = _multicast_buffer((world * hkv_r * G, length, D), dtype, dev, None)
+        good = 1
+        try:
+            mc = _multicast_buffer((world * hkv_r * G, length, D), dtype, dev, None)
+        except Exception as exc:  # no symmetric memory / multicast on this node
+            print(f"multicast reassembly unavailable ({exc}); using NCCL all-gather",
+                  file=sys.stderr)
+            mc, good = None, 0
+        agree = torch.tensor([good], dtype=torch.int32, device=dev)
+        dist.all_reduce(agree, op=dist.ReduceOp.MIN)   # every rank takes the same path
+        if int(agree.item()) == 0:
+            mc = None
     mc_args = (mc[2], rank * hkv_r * G, world * hkv_r * G) if mc else None
 
     def step():
