@@ -273,15 +273,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         good = __shfl_sync(0xffffffffu, good, 0);
         if (!good) return false;
-        constexpr int kChunks = D / 8;   // 16-byte chunks per row
+        constexpr int kChunks = D / 8;   // 16-byte chunks per tile row (past a.D: zeros)
         for (int idx = lane; idx < 128 * kChunks; idx += 32) {
           const int e = idx / kChunks, cidx = idx % kChunks;
           const int hh = cidx >> 3, cc = cidx & 7;
           const uint32_t off = hh * 16384 + e * 128 + ((cc ^ (e & 7)) << 4);
           uint4 kvk = make_uint4(0, 0, 0, 0), kvv = make_uint4(0, 0, 0, 0);
-          if (e < rec.nvalid) {
+          if (e < rec.nvalid && cidx * 8 < a.D) {
             const int blk = clampi(a.pr_ids[lrow + rec.kstart + e], 0, a.Nb - 1);
-            const long long src = ((long long)ck.h * a.Nb + blk) * D + cidx * 8;
+            const long long src = ((long long)ck.h * a.Nb + blk) * a.D + cidx * 8;
             const float4* fk = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.pk) + src);
             const float4* fv = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.pv) + src);
             const float4 k0 = __ldg(fk), k1 = __ldg(fk + 1), v0 = __ldg(fv), v1 = __ldg(fv + 1);
@@ -792,9 +792,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int P = P0 + rr;
               const long long head = a.mc_head_offset + ck.h * a.G + P / a.tile_q;
               const long long pos = (long long)ck.t * a.tile_q + P % a.tile_q;
-              char* dst = reinterpret_cast<char*>(a.out_mc) +
-                          ((head * a.Lq_pad + pos) * D + ob * 64 + cc * 8) * 2;
-              multimem_st16(dst, v);
+              if (ob * 64 + cc * 8 < a.D) {   // head_dim 96 runs on the 128-wide tiles
+                char* dst = reinterpret_cast<char*>(a.out_mc) +
+                            ((head * a.Lq_pad + pos) * a.D + ob * 64 + cc * 8) * 2;
+                multimem_st16(dst, v);
+              }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&q_empty[qs]));
@@ -847,7 +849,7 @@ size_t smem_bytes() {
 
 bool attn_tc_supported(const AttnArgs& a) {
   if (a.dt != DT_BF16 && a.dt != DT_F16) return false;
-  if (a.D != 64 && a.D != 128) return false;
+  if (a.D != 64 && a.D != 96 && a.D != 128) return false;
   if (a.pooled_dt != a.dt && a.pooled_dt != DT_F32) return false;
   if (a.block_k % 128 != 0) return false;
   if (!(a.scale_log2 > 0.f)) return false;
@@ -906,8 +908,11 @@ cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, int* sched, cud
   }
   if (a.D == 64 && a.dt == DT_BF16) FPV2_ATTN_LAUNCH(64, DT_BF16)
   else if (a.D == 64 && a.dt == DT_F16) FPV2_ATTN_LAUNCH(64, DT_F16)
-  else if (a.D == 128 && a.dt == DT_BF16) FPV2_ATTN_LAUNCH(128, DT_BF16)
-  else if (a.D == 128 && a.dt == DT_F16) FPV2_ATTN_LAUNCH(128, DT_F16)
+  // head_dim 96 runs on the 128-wide tiles: the tensor maps have the real
+  // extent, so TMA fills columns 96..127 of Q/K/V with zeros (QK unchanged),
+  // PV runs with N = 96, and the output store clips at column 96.
+  else if (a.D >= 96 && a.dt == DT_BF16) FPV2_ATTN_LAUNCH(128, DT_BF16)
+  else if (a.D >= 96 && a.dt == DT_F16) FPV2_ATTN_LAUNCH(128, DT_F16)
   else return cudaErrorInvalidValue;
 #undef FPV2_ATTN_LAUNCH
   return cudaGetLastError();

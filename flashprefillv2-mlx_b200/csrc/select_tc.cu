@@ -541,7 +541,7 @@ int pick_k_stages(int Nb) {
 bool select_tc_supported(const SelectGeom& g, int dt) {
   if (dt != DT_BF16 && dt != DT_F16) return false;
   if (!(g.scale > 0.f)) return false;
-  if (g.D != 64 && g.D != 128) return false;
+  if (g.D != 64 && g.D != 96 && g.D != 128) return false;   // 96: zero-padded 128-wide tiles
   if (g.Nb > kMaxNb || g.Nb <= 0) return false;
   if ((g.D == 64 ? pick_k_stages<64>(g.Nb) : pick_k_stages<128>(g.Nb)) == 0) return false;
   const int R = g.G * g.tile_q;
