@@ -42,8 +42,7 @@
 //              quarter (thread = query row), each owning one 64-key half of
 //              every S tile and its accumulator O_h; in the epilogue each
 //              writes half of the output columns.
-#include "common.cuh"
-#include "kernels.h"
+#include "attn_common.cuh"
 
 namespace fpv2 {
 
@@ -53,23 +52,6 @@ constexpr int kThreads = 320;   // producer, MMA, 8 softmax warps
 constexpr int kStages = 2;      // K/V tiles and S buffers
 constexpr int kRecs = 8;        // item records in flight
 constexpr int kTmemCols = 512;
-// Lazy-rescale threshold in log2 units: P = 2^(x - m_h) stays below 2^T, which
-// the 16-bit P of the PV product represents (fp16 max 65504 < 2^16).
-template <int DT> struct RescaleT { static constexpr float value = 16.0f; };
-template <> struct RescaleT<DT_F16> { static constexpr float value = 15.0f; };
-constexpr int kMaskWordsMax = 64;           // pooled-entry mask of one work item (Nb <= 2048)
-
-enum : int { KIND_SEL = 0, KIND_POOL = 1, KIND_CORR = 2, KIND_EMPTY = 3, KIND_DONE = 4 };
-
-struct Rec {
-  int kind;
-  int kstart;     // SEL: first key; POOL: first pooled row; CORR: first list entry
-  int nvalid;     // CORR: valid list entries in this chunk
-  int flags;      // bit 0: first item of the work item, bit 1: last item
-  int w;          // work item index
-  uint32_t mask[4];   // POOL: entry e is a pruned block when bit (e & 31) of mask[e >> 5]
-};
-
 template <int D>
 struct Cfg {
   static constexpr int kHalves = D / 64;
@@ -77,42 +59,6 @@ struct Cfg {
   static constexpr int kOCol = 0;                  // O_h at columns [128 h, 128 h + D)
   static constexpr int kSCol = 256;                // S buffers at 256, 384
 };
-
-struct Params {
-  AttnArgs a;
-  int nch;          // 128-row chunks per tile
-  int items;        // total work items
-  uint32_t idesc_qk, idesc_pv;
-  int* sched;       // work counter (zeroed before launch); null = static round robin
-  int* status;
-  long long budget;
-};
-
-struct Chunk {
-  int h, t, c;
-  int g0, p0;               // first head / position of the chunk inside the tile
-  long long abs_last;       // last valid absolute query position of the chunk
-};
-
-__device__ __forceinline__ Chunk make_chunk(const Params& p, int w) {
-  const AttnArgs& a = p.a;
-  Chunk ck;
-  const int per_t = a.Hkv * p.nch;
-  ck.t = a.Nt - 1 - w / per_t;   // latest tiles (most causal work) first
-  const int r = w % per_t;
-  ck.h = r / p.nch;
-  ck.c = r % p.nch;
-  const int P0 = ck.c * 128;
-  ck.g0 = P0 / a.tile_q;
-  ck.p0 = P0 % a.tile_q;
-  const long long span = min(a.tile_q, 128);
-  const long long last_row =
-      min((long long)ck.t * a.tile_q + ck.p0 + span, (long long)a.valid_lq) - 1;
-  ck.abs_last = (long long)a.offset + last_row;
-  return ck;
-}
-
-__device__ __forceinline__ int clampi(int x, int lo, int hi) { return min(max(x, lo), hi); }
 
 template <int D, int DT>
 __global__ void __launch_bounds__(kThreads, 1)

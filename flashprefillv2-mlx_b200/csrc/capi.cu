@@ -483,9 +483,15 @@ int run_sparse_attention(const void* q, const void* k, const void* v, const void
                      : nullptr;
     e = launch_attn_tc(a, tc_launch(*d), sched, s);
     if (e != cudaSuccess) return cuda_fail(e, "attn_tc launch");
+  } else if (aligned && attn_wide_supported(a)) {
+    int* sched = (workspace != nullptr && workspace_bytes >= (int64_t)sizeof(int))
+                     ? reinterpret_cast<int*>(workspace)
+                     : nullptr;
+    e = launch_attn_wide(a, tc_launch(*d), sched, s);
+    if (e != cudaSuccess) return cuda_fail(e, "attn_wide launch");
   } else if (out_mc != nullptr) {
     return fail(FPV2_ERR_UNSUPPORTED,
-                "multicast output needs the tcgen05 path (bf16/fp16, head_dim 64/128, aligned)");
+                "multicast output needs the tcgen05 path (bf16/fp16, head_dim 64/96/128/256, aligned)");
   } else {
     e = launch_attn_generic(a, s);
     if (e != cudaSuccess) return cuda_fail(e, "attn_generic launch");
@@ -554,7 +560,7 @@ int fpv2_fast_path_mask(int dtype, int32_t q_heads, int32_t kv_heads, int32_t he
   a.scale_log2 = 1.f;   // any positive softmax scale
   int m = 0;
   if (select_tc_supported(g, dtype)) m |= 1;
-  if (attn_tc_supported(a)) m |= 2;
+  if (attn_tc_supported(a) || attn_wide_supported(a)) m |= 2;
   return m;
 }
 

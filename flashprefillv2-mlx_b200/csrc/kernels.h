@@ -102,6 +102,9 @@ cudaError_t launch_select_tc(const SelectTcArgs& a, const void* q, const void* p
 // counter; it is zeroed on `stream` before the launch. Null = static schedule.
 bool attn_tc_supported(const AttnArgs& a);
 cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, int* sched, cudaStream_t stream);
+// attn_wide.cu: the same for head_dim 256 (one softmax warp per row quarter).
+bool attn_wide_supported(const AttnArgs& a);
+cudaError_t launch_attn_wide(const AttnArgs& a, const TcLaunch& L, int* sched, cudaStream_t stream);
 
 // selftest.cu: bounded-wait failure detection.
 cudaError_t launch_wait_selftest(const TcLaunch& L, cudaStream_t stream);

@@ -44,8 +44,8 @@ constexpr int kSmemLimit = 227 * 1024;
 template <int D>
 struct Cfg {
   static constexpr int kHalves = D / 64;
-  static constexpr int kQStages = 2;
-  static constexpr int kKStagesMax = (D == 64) ? 8 : 4;   // pooled-K ring (runtime count)
+  static constexpr int kQStages = (D == 256) ? 1 : 2;   // a 256-wide Q chunk is 64 KB
+  static constexpr int kKStagesMax = (D == 64) ? 8 : (D == 256 ? 2 : 4);   // pooled-K ring (runtime count)
   static constexpr int kQBytes = 128 * D * 2;   // up to 128 rows per chunk
   static constexpr int kKBytes = 128 * D * 2;
 };
@@ -541,9 +541,11 @@ int pick_k_stages(int Nb) {
 bool select_tc_supported(const SelectGeom& g, int dt) {
   if (dt != DT_BF16 && dt != DT_F16) return false;
   if (!(g.scale > 0.f)) return false;
-  if (g.D != 64 && g.D != 96 && g.D != 128) return false;   // 96: zero-padded 128-wide tiles
+  if (g.D != 64 && g.D != 96 && g.D != 128 && g.D != 256) return false;   // 96: zero-padded 128-wide tiles
   if (g.Nb > kMaxNb || g.Nb <= 0) return false;
-  if ((g.D == 64 ? pick_k_stages<64>(g.Nb) : pick_k_stages<128>(g.Nb)) == 0) return false;
+  const int ks = g.D == 64 ? pick_k_stages<64>(g.Nb)
+                 : (g.D == 256 ? pick_k_stages<256>(g.Nb) : pick_k_stages<128>(g.Nb));
+  if (ks == 0) return false;
   const int R = g.G * g.tile_q;
   if (R >= 128) {
     if (R % 128) return false;
@@ -597,6 +599,13 @@ cudaError_t launch_select_tc(const SelectTcArgs& a, const void* q, const void* p
                              (int)smem);
     if (e != cudaSuccess) return e;
     select_tc_kernel<64><<<grid, kThreads, smem, stream>>>(tq, tk, p);
+  } else if (g.D == 256) {
+    p.k_stages = pick_k_stages<256>(g.Nb);
+    const size_t smem = smem_bytes<256>(g.Nb, p.k_stages);
+    e = cudaFuncSetAttribute(select_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    if (e != cudaSuccess) return e;
+    select_tc_kernel<256><<<grid, kThreads, smem, stream>>>(tq, tk, p);
   } else {
     p.k_stages = pick_k_stages<128>(g.Nb);
     const size_t smem = smem_bytes<128>(g.Nb, p.k_stages);

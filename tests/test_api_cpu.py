@@ -42,7 +42,8 @@ def test_fast_path_selection_rules_without_gpu():
     assert _lib.fast_path_mask(torch.float16, 64, 8, 128, 128, 16, 1024) == 3
     assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 128, 128, 128, 16) == 3   # direct tile_q 128
     assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 96, 128, 32, 16) == 3   # zero-padded 128-wide tiles
-    assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 256, 128, 32, 16) == 0
+    assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 256, 128, 32, 16) == 3
+    assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 48, 128, 32, 16) == 0
     assert _lib.fast_path_mask(torch.bfloat16, 4, 2, 64, 16, 16, 4) == 1       # select tc, attn generic
     assert _lib.fast_path_mask(torch.float32, 8, 2, 128, 128, 32, 16) == 0
 

@@ -101,7 +101,8 @@ SELECT_CASES = [
     (2048, 8, 2, 64, torch.bfloat16, 0.1, 3),
     (2048, 16, 2, 128, torch.bfloat16, 0.05, 4),    # G = 8, tile_q = 16
     (2048, 8, 2, 96, torch.bfloat16, 0.1, 5),       # tensor cores on zero-padded 128-wide tiles
-    (2048, 8, 2, 256, torch.bfloat16, 0.1, 6),      # generic CUDA-core path
+    (2048, 8, 2, 256, torch.bfloat16, 0.1, 6),      # 256-wide chunks, single-buffered Q
+    (2048, 8, 2, 48, torch.bfloat16, 0.1, 7),       # generic CUDA-core path
     (1024, 8, 2, 128, torch.float32, 0.1, 6),       # generic, fp32
 ]
 
@@ -277,7 +278,8 @@ ATTN_CASES = [
     (128, torch.bfloat16, True, 0.15, 128),   # direct 128-position tiles: 4 chunks per tile
     (96, torch.bfloat16, True, 0.15, None),   # tensor cores on zero-padded 128-wide tiles
     (96, torch.float16, False, 0.1, None),
-    (256, torch.bfloat16, True, 0.15, None),  # generic path
+    (256, torch.bfloat16, True, 0.15, None),  # attn_wide_kernel
+    (256, torch.float16, False, 0.1, None),
 ]
 
 
@@ -349,7 +351,8 @@ def test_alpha_zero_equals_dense_causal_attention():
 def test_fast_path_mask():
     assert _lib.fast_path_mask(torch.bfloat16, 32, 8, 128, 128, 32, 512) == 3
     assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 96, 128, 32, 16) == 3
-    assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 256, 128, 32, 16) == 0
+    assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 256, 128, 32, 16) == 3
+    assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 48, 128, 32, 16) == 0
 
 
 def test_bounded_wait_times_out_and_context_survives():
