@@ -30,14 +30,15 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _inputs(length: int, hq: int, hkv: int):
+def _inputs(length: int, hq: int, hkv: int, d: int):
     from tests.synthetic import topic_qkv
 
-    q, k, v = topic_qkv(length=length, query_heads=hq, kv_heads=hkv, seed=21, dtype=torch.bfloat16)
+    q, k, v = topic_qkv(length=length, query_heads=hq, kv_heads=hkv, head_dim=d, seed=21,
+                        dtype=torch.bfloat16)
     return q[None], k[None], v[None]
 
 
-def _worker(rank: int, world: int, port: int, length: int, hq: int, hkv: int, queue) -> None:
+def _worker(rank: int, world: int, port: int, length: int, hq: int, hkv: int, d: int, queue) -> None:
     import torch.distributed as dist
 
     try:
@@ -50,16 +51,16 @@ def _worker(rank: int, world: int, port: int, length: int, hq: int, hkv: int, qu
         dev = torch.device("cuda", rank)
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                                 device_id=dev)
-        q, k, v = _inputs(length, hq, hkv)
+        q, k, v = _inputs(length, hq, hkv, d)
         sh = head_shard(hq, hkv, world, rank)
         ql, kl, vl = (t.to(dev) for t in shard_inputs(q, k, v, sh))
         from fpv2.shard import _SYMM_BUFFERS
 
         cfg = fpv2.FPV2Config(alpha=0.1)
-        ref = fpv2.fpv2_sdpa(q.to(dev), k.to(dev), v.to(dev), scale=128 ** -0.5, config=cfg)
+        ref = fpv2.fpv2_sdpa(q.to(dev), k.to(dev), v.to(dev), scale=d ** -0.5, config=cfg)
         report = []
         for fused in (False, True, True):   # NCCL, then the fused path twice (buffer reuse)
-            out = head_parallel_sdpa(ql, kl, vl, scale=128 ** -0.5, config=cfg, fused=fused)
+            out = head_parallel_sdpa(ql, kl, vl, scale=d ** -0.5, config=cfg, fused=fused)
             torch.cuda.synchronize(dev)
             diff = (out.float() - ref.float()).abs().max().item()
             report.append(f"{diff}")
@@ -72,12 +73,13 @@ def _worker(rank: int, world: int, port: int, length: int, hq: int, hkv: int, qu
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("length,hq,hkv", [(8192, 32, 8), (4096 + 384, 16, 4)])
-def test_head_parallel_two_gpus_matches_single_gpu(length, hq, hkv):
+@pytest.mark.parametrize("length,hq,hkv,d", [(8192, 32, 8, 128), (4096 + 384, 16, 4, 128),
+                                             (4096, 8, 2, 256), (4096, 8, 2, 96)])
+def test_head_parallel_two_gpus_matches_single_gpu(length, hq, hkv, d):
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, length, hq, hkv, queue)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, length, hq, hkv, d, queue)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(queue.get(timeout=300) for _ in procs)
