@@ -227,7 +227,7 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tiles", type=int, default=2048,
                     help="latest tiles of a KV head per CPU sample (the reference arm uses 1/8)")
-    ap.add_argument("--cpu-heads", type=int, default=2, help="KV heads in the CPU baseline sample")
+    ap.add_argument("--cpu-heads", type=int, default=3, help="KV heads in the CPU baseline sample")
     return ap.parse_args(argv)
 
 
