@@ -551,9 +551,10 @@ def main(argv=None) -> int:
         kh = ks[None].pin_memory()
         vh = vs[None].pin_memory()
         oh = torch.empty((1, hkv_r * G, length, D), dtype=dtype).pin_memory()
-        qb = torch.empty_like(qd)
-        kb = torch.empty_like(kd)
-        vb = torch.empty_like(vd)
+        if world > 1:   # one GPU streams through fpv2.sdpa_from_host's own buffers
+            qb = torch.empty_like(qd)
+            kb = torch.empty_like(kd)
+            vb = torch.empty_like(vd)
 
         def e2e_step():
             if world == 1:
