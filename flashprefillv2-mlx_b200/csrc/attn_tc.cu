@@ -44,6 +44,8 @@
 //              writes half of the output columns.
 #include "attn_common.cuh"
 
+#include <algorithm>
+
 namespace fpv2 {
 
 namespace {
@@ -192,22 +194,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           const CUtensorMap* mk = rec.kind == KIND_SEL ? &tmap_k : &tmap_pk;
           const CUtensorMap* mv = rec.kind == KIND_SEL ? &tmap_v : &tmap_pv;
+          const bool paged = rec.kind == KIND_SEL && a.block_table != nullptr;
+          // One 128-row tile: a single 3-D box per 64 features, or, from a page
+          // pool, one 4-D box per page the 128 keys span.
+          auto load_tile = [&](uint32_t dst, const CUtensorMap* m, uint32_t bar) {
+            mbar_arrive_expect_tx(bar, (uint32_t)C::kTileBytes);
+            if (!paged) {
+#pragma unroll
+              for (int hh = 0; hh < C::kHalves; ++hh)
+                tma_load_3d(dst + hh * 16384, m, bar, hh * 64, rec.kstart, ck.h);
+              return;
+            }
+            const int rows = min(a.page_size, 128);
+            for (int r0 = 0; r0 < 128; r0 += rows) {
+              const int key = rec.kstart + r0;
+              const int page = clampi(a.block_table[min(key / a.page_size, a.table_len - 1)], 0,
+                                      a.num_pages - 1);
+#pragma unroll
+              for (int hh = 0; hh < C::kHalves; ++hh)
+                tma_load_4d(dst + hh * 16384 + r0 * 128, m, bar, hh * 64, ck.h, key % a.page_size,
+                            page);
+            }
+          };
           good = mbar_wait(smem_u32(&k_empty[st]), par, wc);
           if (good) {
-            const uint32_t kb = smem_u32(&k_full[st]);
-            mbar_arrive_expect_tx(kb, (uint32_t)C::kTileBytes);
-#pragma unroll
-            for (int hh = 0; hh < C::kHalves; ++hh)
-              tma_load_3d(kst + hh * 16384, mk, kb, hh * 64, rec.kstart, ck.h);
+            load_tile(kst, mk, smem_u32(&k_full[st]));
             good = mbar_wait(smem_u32(&v_empty[st]), par, wc);
           }
-          if (good) {
-            const uint32_t vb = smem_u32(&v_full[st]);
-            mbar_arrive_expect_tx(vb, (uint32_t)C::kTileBytes);
-#pragma unroll
-            for (int hh = 0; hh < C::kHalves; ++hh)
-              tma_load_3d(vst + hh * 16384, mv, vb, hh * 64, rec.kstart, ck.h);
-          }
+          if (good) load_tile(vst, mv, smem_u32(&v_full[st]));
         }
         good = __shfl_sync(0xffffffffu, good, 0);
         if (!good) return false;
@@ -803,6 +817,12 @@ bool attn_tc_supported(const AttnArgs& a) {
   const int R = a.G * a.tile_q;
   if (R % 128 != 0) return false;
   if (a.tile_q % 128 != 0 && 128 % a.tile_q != 0) return false;
+  if (a.block_table != nullptr) {   // pages of whole 8-row swizzle atoms, tiles within or across pages
+    if (a.page_size < 8 || a.page_size % 8 != 0) return false;
+    if (128 % a.page_size != 0 && a.page_size % 128 != 0) return false;
+    if (a.num_pages <= 0 || a.table_len <= 0) return false;
+    if ((long long)a.table_len * a.page_size < a.Lk_pad) return false;
+  }
   return true;
 }
 
@@ -828,15 +848,23 @@ cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, int* sched, cud
   if (!encode_tmap_3d(&to, a.out_mc != nullptr ? a.q : a.out, a.dt, a.D, a.Lq_pad, a.Hq, 64,
                       box_rows, box_heads))
     return cudaErrorInvalidValue;
-  if (!encode_tmap_3d(&tk, a.k, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return cudaErrorInvalidValue;
-  if (!encode_tmap_3d(&tv, a.v, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return cudaErrorInvalidValue;
+  if (a.block_table != nullptr) {   // page pools [pages, page_size, Hkv, D]
+    const uint32_t rows = (uint32_t)std::min(a.page_size, 128);
+    if (!encode_tmap_pages(&tk, a.k, a.dt, a.D, a.Hkv, a.page_size, a.num_pages, rows) ||
+        !encode_tmap_pages(&tv, a.v, a.dt, a.D, a.Hkv, a.page_size, a.num_pages, rows))
+      return cudaErrorInvalidValue;
+  } else {
+    if (!encode_tmap_3d(&tk, a.k, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return cudaErrorInvalidValue;
+    if (!encode_tmap_3d(&tv, a.v, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return cudaErrorInvalidValue;
+  }
   // Pooled tiles (only read when pooled K/V share the compute dtype).
   const bool pooled_ok = a.corr && a.pooled_dt == a.dt;
-  if (!encode_tmap_3d(&tpk, pooled_ok ? a.pk : a.k, a.dt, a.D, pooled_ok ? a.Nb : a.Lk_pad, a.Hkv,
-                      64, 128, 1))
+  // (pooled tiles unused: q stands in for the pooled tensors)
+  if (!encode_tmap_3d(&tpk, pooled_ok ? a.pk : a.q, a.dt, a.D, pooled_ok ? a.Nb : a.Lq_pad,
+                      pooled_ok ? a.Hkv : a.Hq, 64, 128, 1))
     return cudaErrorInvalidValue;
-  if (!encode_tmap_3d(&tpv, pooled_ok ? a.pv : a.v, a.dt, a.D, pooled_ok ? a.Nb : a.Lk_pad, a.Hkv,
-                      64, 128, 1))
+  if (!encode_tmap_3d(&tpv, pooled_ok ? a.pv : a.q, a.dt, a.D, pooled_ok ? a.Nb : a.Lq_pad,
+                      pooled_ok ? a.Hkv : a.Hq, 64, 128, 1))
     return cudaErrorInvalidValue;
   const int grid = max(1, min(L.num_sms, p.items));
   cudaError_t e = cudaSuccess;

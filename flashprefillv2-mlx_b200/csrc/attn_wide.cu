@@ -751,6 +751,7 @@ size_t wide_smem_bytes() {
 bool attn_wide_supported(const AttnArgs& a) {
   if (a.dt != DT_BF16 && a.dt != DT_F16) return false;
   if (a.D != kD) return false;
+  if (a.block_table != nullptr) return false;   // paged K/V: head_dim up to 128
   if (a.pooled_dt != a.dt && a.pooled_dt != DT_F32) return false;
   if (a.block_k % 128 != 0) return false;
   if (!(a.scale_log2 > 0.f)) return false;

@@ -136,6 +136,23 @@ bool encode_tmap_3d(CUtensorMap* map, const void* base, int dt, uint64_t d0, uin
   return r == CUDA_SUCCESS;
 }
 
+bool encode_tmap_pages(CUtensorMap* map, const void* base, int dt, uint64_t D, uint64_t heads,
+                       uint64_t page_size, uint64_t pages, uint32_t rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  const size_t es = dt_size(dt);
+  cuuint64_t dims[4] = {D, heads, page_size, pages};
+  cuuint64_t strides[3] = {D * es, heads * D * es, page_size * heads * D * es};
+  cuuint32_t box[4] = {64, 1, rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType ty = dt == DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, ty, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // Shared validation of the selection geometry (fpv2/selection.py:83-106).
 static int check_select_geom(const SelectGeom& g) {
   if (g.Hkv <= 0 || g.Hq <= 0 || g.Hq % g.Hkv)
@@ -400,6 +417,12 @@ namespace fpv2 {
 namespace {
 
 // Shared body of fpv2_sparse_attention and fpv2_sparse_attention_multicast.
+// K/V in page pools (fpv2_sparse_attention_paged); null for contiguous K/V.
+struct PagedKV {
+  const int32_t* table;
+  int32_t table_len, num_pages, page_size;
+};
+
 int run_sparse_attention(const void* q, const void* k, const void* v, const void* pooled_k,
                          const void* pooled_v, int pooled_dtype, const int32_t* selected_ids,
                          const int32_t* selected_counts, const int32_t* pruned_ids,
@@ -409,7 +432,7 @@ int run_sparse_attention(const void* q, const void* k, const void* v, const void
                          int32_t key_length, float scale, int32_t block_k, int32_t tile_q,
                          int32_t mean_correction, void* out, void* out_mc, int32_t head_offset,
                          int32_t heads_total, void* workspace, int64_t workspace_bytes,
-                         void* stream) {
+                         void* stream, const PagedKV* paged = nullptr) {
   if (dtype != DT_F16 && dtype != DT_BF16)
     return fail(FPV2_ERR_INVALID_ARGUMENT, "q, k, and v must share float16 or bfloat16 dtype");
   if (pooled_dtype != dtype && pooled_dtype != DT_F32)
@@ -433,6 +456,13 @@ int run_sparse_attention(const void* q, const void* k, const void* v, const void
   if (out_mc != nullptr &&
       (head_offset < 0 || heads_total < q_heads || head_offset > heads_total - q_heads))
     return fail(FPV2_ERR_INVALID_ARGUMENT, "multicast output heads out of range");
+  if (paged != nullptr) {
+    if (paged->table == nullptr || paged->page_size <= 0 || paged->num_pages <= 0 ||
+        paged->table_len <= 0)
+      return fail(FPV2_ERR_INVALID_ARGUMENT, "paged K/V needs a block table, pages and a page size");
+    if ((long long)paged->table_len * paged->page_size < padded_k_len)
+      return fail(FPV2_ERR_INVALID_ARGUMENT, "block table does not cover the padded key length");
+  }
   DeviceInfo* d = nullptr;
   int rc = device_info(&d);
   if (rc != FPV2_OK) return rc;
@@ -468,6 +498,12 @@ int run_sparse_attention(const void* q, const void* k, const void* v, const void
   a.out_mc = out_mc;
   a.mc_head_offset = head_offset;
   a.mc_heads = heads_total;
+  if (paged != nullptr) {
+    a.block_table = paged->table;
+    a.page_size = paged->page_size;
+    a.num_pages = paged->num_pages;
+    a.table_len = paged->table_len;
+  }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool aligned = reinterpret_cast<uintptr_t>(q) % 16 == 0 &&
                        reinterpret_cast<uintptr_t>(k) % 16 == 0 &&
@@ -489,6 +525,10 @@ int run_sparse_attention(const void* q, const void* k, const void* v, const void
                      : nullptr;
     e = launch_attn_wide(a, tc_launch(*d), sched, s);
     if (e != cudaSuccess) return cuda_fail(e, "attn_wide launch");
+  } else if (paged != nullptr) {
+    return fail(FPV2_ERR_UNSUPPORTED,
+                "paged K/V needs the tcgen05 path (bf16/fp16, head_dim 64/96/128, aligned, block_k a "
+                "multiple of 128, page_size a multiple of 8 that divides 128 or is a multiple of 128)");
   } else if (out_mc != nullptr) {
     return fail(FPV2_ERR_UNSUPPORTED,
                 "multicast output needs the tcgen05 path (bf16/fp16, head_dim 64/96/128/256, aligned)");
@@ -535,6 +575,48 @@ int fpv2_sparse_attention_multicast(
                                     query_length, key_length, scale, block_k, tile_q,
                                     mean_correction, nullptr, out_multicast, head_offset,
                                     heads_total, workspace, workspace_bytes, stream);
+}
+
+int fpv2_sparse_attention_paged(
+    const void* q, const void* k_pages, const void* v_pages, const int32_t* block_table,
+    int32_t table_len, int32_t num_pages, int32_t page_size, const void* pooled_k,
+    const void* pooled_v, int pooled_dtype, const int32_t* selected_ids,
+    const int32_t* selected_counts, const int32_t* pruned_ids, const int32_t* pruned_counts,
+    int dtype, int32_t q_heads, int32_t kv_heads, int32_t padded_q_len, int32_t padded_k_len,
+    int32_t head_dim, int32_t offset, int32_t query_length, int32_t key_length, float scale,
+    int32_t block_k, int32_t tile_q, int32_t mean_correction, void* out, void* workspace,
+    int64_t workspace_bytes, void* stream) {
+  const fpv2::PagedKV paged{block_table, table_len, num_pages, page_size};
+  return fpv2::run_sparse_attention(q, k_pages, v_pages, pooled_k, pooled_v, pooled_dtype,
+                                    selected_ids, selected_counts, pruned_ids, pruned_counts, dtype,
+                                    q_heads, kv_heads, padded_q_len, padded_k_len, head_dim, offset,
+                                    query_length, key_length, scale, block_k, tile_q,
+                                    mean_correction, out, nullptr, 0, 0, workspace, workspace_bytes,
+                                    stream, &paged);
+}
+
+int fpv2_pool_pages(const void* pages, const int32_t* block_table, int32_t table_len,
+                    int32_t num_pages, int32_t page_size, int32_t kv_heads, int32_t head_dim,
+                    int32_t length, int32_t block_size, int dtype, void* out, int out_dtype,
+                    void* stream) {
+  using namespace fpv2;
+  if (dtype != DT_F16 && dtype != DT_BF16)
+    return fail(FPV2_ERR_INVALID_ARGUMENT, "page pools must be float16 or bfloat16");
+  if (out_dtype != DT_F16 && out_dtype != DT_BF16 && out_dtype != DT_F32)
+    return fail(FPV2_ERR_INVALID_ARGUMENT, "unsupported output dtype");
+  if (!pages || !block_table || !out) return fail(FPV2_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (kv_heads <= 0 || head_dim <= 0 || head_dim % 8 || page_size <= 0 || num_pages <= 0 ||
+      table_len <= 0 || block_size <= 0)
+    return fail(FPV2_ERR_INVALID_ARGUMENT, "invalid page pool geometry");
+  if (length <= 0 || length % block_size)
+    return fail(FPV2_ERR_INVALID_ARGUMENT, "sequence length must be divisible by block size");
+  if ((long long)table_len * page_size < length)
+    return fail(FPV2_ERR_INVALID_ARGUMENT, "block table does not cover the sequence");
+  PagedPoolArgs a{pages, block_table, table_len, num_pages, page_size, kv_heads, head_dim, length,
+                  block_size, out};
+  cudaError_t e = launch_pool_pages(a, dtype, out_dtype, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "pool_pages launch");
+  return FPV2_OK;
 }
 
 int fpv2_fast_path_mask(int dtype, int32_t q_heads, int32_t kv_heads, int32_t head_dim,

@@ -17,6 +17,16 @@ struct PoolArgs {
 cudaError_t launch_pool(const PoolArgs& a, int ntensors, int dt_in, int dt_out,
                         cudaStream_t stream);
 
+// Block means of a sequence whose rows live in a page pool [pages, page_size,
+// heads, D]: out [heads, length / bs, D], the same exact definition as above.
+struct PagedPoolArgs {
+  const void* pages;
+  const int32_t* table;
+  int table_len, num_pages, page_size, heads, D, length, bs;
+  void* out;
+};
+cudaError_t launch_pool_pages(const PagedPoolArgs& a, int dt_in, int dt_out, cudaStream_t stream);
+
 // ---- selection geometry shared by all selection kernels -----------------
 struct SelectGeom {
   int Hq, Hkv, G, Lq_pad, Nb, D, Nt;
@@ -70,6 +80,13 @@ struct AttnArgs {
   void* out_mc = nullptr;
   int mc_head_offset = 0;
   int mc_heads = 0;
+  // Optional paged K/V: k and v point at page pools [num_pages, page_size, Hkv,
+  // D]; key position p is row p % page_size of page block_table[p / page_size].
+  // Null: k and v are [Hkv, Lk_pad, D].
+  const int32_t* block_table = nullptr;
+  int page_size = 0;
+  int num_pages = 0;
+  int table_len = 0;
 };
 cudaError_t launch_attn_generic(const AttnArgs& a, cudaStream_t stream);
 
@@ -112,5 +129,9 @@ cudaError_t launch_wait_selftest(const TcLaunch& L, cudaStream_t stream);
 // tensor map helper (capi.cu)
 bool encode_tmap_3d(CUtensorMap* map, const void* base, int dt, uint64_t d0, uint64_t d1,
                     uint64_t d2, uint32_t b0, uint32_t b1, uint32_t b2);
+// Page pool [pages, page_size, heads, D] as a 4-D map with dims (D, heads,
+// page_size, pages) and a box of 64 features x 1 head x `rows` rows x 1 page.
+bool encode_tmap_pages(CUtensorMap* map, const void* base, int dt, uint64_t D, uint64_t heads,
+                       uint64_t page_size, uint64_t pages, uint32_t rows);
 
 }  // namespace fpv2

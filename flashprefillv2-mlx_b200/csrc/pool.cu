@@ -229,6 +229,64 @@ cudaError_t launch_pool_t(const PoolArgs& a, int ntensors, cudaStream_t stream) 
   return cudaGetLastError();
 }
 
+
+// ---- paged sequences ---------------------------------------------------------
+// One CTA per (head, block); rows of the block are looked up in the block table
+// (row p of the sequence = row p % page_size of page table[p / page_size]).
+template <int DT_IN, int DT_OUT>
+__global__ void __launch_bounds__(kPoolThreads)
+    pool_pages_kernel(PagedPoolArgs a) {
+  using Tout = typename Elem<DT_OUT>::T;
+  const int nblk = a.length / a.bs;
+  const int head = blockIdx.x / nblk;
+  const int blk = blockIdx.x % nblk;
+  const int cpr = a.D / 8;                          // 16-byte chunks per row
+  const int rows_in_flight = kPoolThreads / cpr;
+  const int tid = threadIdx.x;
+  const int c = tid % cpr, rsub = tid / cpr;
+  double acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.0;
+  if (rsub < rows_in_flight) {
+    for (int r = rsub; r < a.bs; r += rows_in_flight) {
+      const int pos = blk * a.bs + r;
+      const int page = min(max(a.table[pos / a.page_size], 0), a.num_pages - 1);
+      const long long row = ((long long)page * a.page_size + pos % a.page_size) * a.heads + head;
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(
+          reinterpret_cast<const uint8_t*>(a.pages) + (row * a.D + c * 8) * 2));
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack2<DT_IN>(w[e]);
+        acc[2 * e] += (double)f.x;
+        acc[2 * e + 1] += (double)f.y;
+      }
+    }
+  }
+  extern __shared__ double pred[];
+  if (rsub < rows_in_flight) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) pred[rsub * a.D + c * 8 + e] = acc[e];
+  }
+  __syncthreads();
+  for (int col = tid; col < a.D; col += kPoolThreads) {
+    double sum = 0.0;
+    for (int j = 0; j < rows_in_flight; ++j) sum += pred[j * a.D + col];
+    const float m = (float)(sum / (double)a.bs);
+    reinterpret_cast<Tout*>(a.out)[((long long)head * nblk + blk) * a.D + col] = Elem<DT_OUT>::from_f(m);
+  }
+}
+
+template <int DT_IN, int DT_OUT>
+cudaError_t launch_pool_pages_t(const PagedPoolArgs& a, cudaStream_t stream) {
+  const int cpr = a.D / 8;
+  if (cpr > kPoolThreads) return cudaErrorInvalidValue;   // threads past whole rows idle
+  const int nblocks = a.heads * (a.length / a.bs);
+  const size_t smem = sizeof(double) * (size_t)(kPoolThreads / cpr) * a.D;
+  pool_pages_kernel<DT_IN, DT_OUT><<<nblocks, kPoolThreads, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_pool(const PoolArgs& a, int ntensors, int dt_in, int dt_out,
@@ -245,6 +303,18 @@ cudaError_t launch_pool(const PoolArgs& a, int ntensors, int dt_in, int dt_out,
   FPV2_POOL_CASE(DT_BF16, DT_F16)
   FPV2_POOL_CASE(DT_F16, DT_BF16)
 #undef FPV2_POOL_CASE
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_pool_pages(const PagedPoolArgs& a, int dt_in, int dt_out, cudaStream_t stream) {
+  if (a.heads <= 0 || a.length / a.bs == 0) return cudaSuccess;
+#define FPV2_PAGES_CASE(I, O) \
+  if (dt_in == I && dt_out == O) return launch_pool_pages_t<I, O>(a, stream);
+  FPV2_PAGES_CASE(DT_BF16, DT_BF16)
+  FPV2_PAGES_CASE(DT_BF16, DT_F32)
+  FPV2_PAGES_CASE(DT_F16, DT_F16)
+  FPV2_PAGES_CASE(DT_F16, DT_F32)
+#undef FPV2_PAGES_CASE
   return cudaErrorInvalidValue;
 }
 

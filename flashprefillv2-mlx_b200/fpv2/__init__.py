@@ -13,6 +13,7 @@ from fpv2.kernel import (
     index_stage,
     sparse_attention,
 )
+from fpv2.paged import pool_pages, sparse_attention_paged
 from fpv2.patch import block_sparsity, disable, enable, fpv2_sdpa, is_enabled
 from fpv2.selection import FPV2Config, block_scores_and_select, density, pool_blocks
 from fpv2.stream import sdpa_from_host
@@ -32,6 +33,8 @@ __all__ = [
     "index_stage",
     "is_enabled",
     "pool_blocks",
+    "pool_pages",
     "sdpa_from_host",
     "sparse_attention",
+    "sparse_attention_paged",
 ]

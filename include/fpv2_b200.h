@@ -164,7 +164,7 @@ FPV2_API int fpv2_sparse_attention(const void* q, const void* k, const void* v, 
  * example torch symmetric memory); this call's query head hq is written to
  * head `head_offset + hq` of every rank's buffer as each output tile
  * completes, with 16-byte multimem stores. Needs the tcgen05 path (bf16/fp16,
- * head_dim 64 or 128, 16-byte aligned pointers), else FPV2_ERR_UNSUPPORTED.
+ * head_dim 64, 96, 128 or 256, 16-byte aligned pointers), else FPV2_ERR_UNSUPPORTED.
  * The caller orders the ranks around the call (a cross-rank barrier after it
  * before reading the buffer, and before reusing it).
  */
@@ -198,6 +198,39 @@ FPV2_API int fpv2_sparse_attention_noalloc(
     int32_t kv_heads, int32_t padded_q_len, int32_t padded_k_len, int32_t head_dim,
     int32_t offset, int32_t query_length, int32_t key_length, float scale, int32_t block_k,
     int32_t tile_q, int32_t mean_correction, void* out, void* stream);
+
+/*
+ * Paged K/V (no counterpart in the reference, whose MLX KV cache is one
+ * contiguous array; this is the serving-side form of the same call): k_pages
+ * and v_pages are page pools [num_pages, page_size, kv_heads, head_dim] in the
+ * token-major layout of paged KV caches, and key position p of the sequence is
+ * row p % page_size of page block_table[p / page_size] (table_len entries,
+ * covering padded_k_len). The block lists, pooled K/V and every other argument
+ * are those of fpv2_sparse_attention (lists hold logical block indices).
+ * Needs the tcgen05 path: bf16/fp16, head_dim 64/96/128, block_k a multiple of
+ * 128, page_size a multiple of 8 that divides 128 or is a multiple of 128;
+ * else FPV2_ERR_UNSUPPORTED. Out-of-range table entries are clamped.
+ */
+FPV2_API int fpv2_sparse_attention_paged(
+    const void* q, const void* k_pages, const void* v_pages, const int32_t* block_table,
+    int32_t table_len, int32_t num_pages, int32_t page_size, const void* pooled_k,
+    const void* pooled_v, int pooled_dtype, const int32_t* selected_ids,
+    const int32_t* selected_counts, const int32_t* pruned_ids, const int32_t* pruned_counts,
+    int dtype, int32_t q_heads, int32_t kv_heads, int32_t padded_q_len, int32_t padded_k_len,
+    int32_t head_dim, int32_t offset, int32_t query_length, int32_t key_length, float scale,
+    int32_t block_k, int32_t tile_q, int32_t mean_correction, void* out, void* workspace,
+    int64_t workspace_bytes, void* stream);
+
+/*
+ * fpv2_pool_blocks for a sequence held in a page pool (see
+ * fpv2_sparse_attention_paged): out [kv_heads, length / block_size, head_dim]
+ * in out_dtype, with the same exact-mean definition. The pool is bf16/fp16,
+ * head_dim a multiple of 8.
+ */
+FPV2_API int fpv2_pool_pages(const void* pages, const int32_t* block_table, int32_t table_len,
+                             int32_t num_pages, int32_t page_size, int32_t kv_heads,
+                             int32_t head_dim, int32_t length, int32_t block_size, int dtype,
+                             void* out, int out_dtype, void* stream);
 
 /*
  * Which kernel family the two stages would use for this shape:

@@ -192,3 +192,25 @@ def test_sdpa_from_host_validates_before_touching_the_gpu():
         fpv2.sdpa_from_host(q[:, :7], k, k, scale=1.0)
     with pytest.raises(ValueError, match="out must be"):
         fpv2.sdpa_from_host(q, k, k, scale=1.0, out=torch.zeros((1, 8, 64, 64), dtype=torch.bfloat16))
+
+
+def test_paged_api_validates_before_touching_the_gpu():
+    import fpv2
+
+    cache = torch.zeros((4, 16, 2, 128), dtype=torch.bfloat16)
+    table = torch.zeros(8, dtype=torch.int32)
+    with pytest.raises(ValueError, match="divisible by block size"):
+        fpv2.pool_pages(cache, table, 128, 100)
+    with pytest.raises(ValueError, match="does not cover"):
+        fpv2.pool_pages(cache, table, 128, 256)
+    with pytest.raises(ValueError, match="int32"):
+        fpv2.pool_pages(cache, table.long(), 128, 128)
+    q = torch.zeros((8, 128, 128), dtype=torch.bfloat16)
+    ids = torch.zeros((2, 4, 1), dtype=torch.int32)
+    cnt = torch.zeros((2, 4), dtype=torch.int32)
+    pk = torch.zeros((2, 1, 128), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="head dimension"):
+        fpv2.sparse_attention_paged(q[..., :32], cache[..., :32], cache[..., :32], table, pk, pk,
+                                    ids, cnt, ids, cnt, scale=1.0)
+    with pytest.raises(ValueError, match="identical shapes"):
+        fpv2.sparse_attention_paged(q, cache, cache[:2], table, pk, pk, ids, cnt, ids, cnt, scale=1.0)
