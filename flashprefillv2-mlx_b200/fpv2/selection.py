@@ -12,7 +12,7 @@ key position of query row zero, so bottom-right chunks select what a single
 shot selects.
 
 The arithmetic runs in ``libfpv2_b200.so``: a tcgen05 kernel for bf16/fp16
-inputs with head_dim 64/128, a CUDA-core kernel otherwise. Query-tile chunking
+inputs with head_dim 64, 96, 128 or 256, a CUDA-core kernel otherwise. Query-tile chunking
 (``score_chunk_tiles``) never changes the result; it only decides whether the
 raw score tensor is returned, as in the reference.
 """
