@@ -47,7 +47,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # full-size single-GPU workload (dram__bytes_read.sum + dram__bytes_write.sum;
 # profiles/dram_traffic_c3.md has the command and the per-kernel split).
 NCU_TRAFFIC_BYTES = {
-    "c3": {"attention": 2883.68e6 + 503.28e6, "index_stage": 268.45e6 + 1.74e6 + 537.58e6 + 57.90e6},
+    "c3": {"attention": 2890.32e6 + 501.88e6, "index_stage": 268.45e6 + 1.33e6 + 537.55e6 + 57.75e6},
 }
 
 CONFIGS = {
