@@ -96,6 +96,16 @@ def retained_attention_flops(sel_ids, sel_counts, pr_counts, *, G, tile_q, block
     return 4.0 * D * total
 
 
+def attention_kernel_name(G: int, tile_q: int, D: int) -> str:
+    """The tensor-core attention kernel the library picks for this tile shape
+    (csrc/attn_pair.cu: chunks of a tile that pair up at the same positions)."""
+    if D == 256:
+        return "attn_wide_kernel"
+    nch = G * tile_q // 128
+    per_group = tile_q // 128 if tile_q >= 128 else 1
+    return "attn_pair_kernel" if nch >= 2 and (nch // per_group) % 2 == 0 else "attn_tc_kernel"
+
+
 def index_stage_bytes(Hq, Hkv, L, D, Nt, Nb, esize=2) -> int:
     """Algorithmic HBM bytes of the fused index stage: read Q, K, V; write pooled K/V,
     two full-width int32 lists and two count arrays."""
@@ -223,6 +233,8 @@ def parse_args(argv=None):
     ap.add_argument("--c4-layers", type=int, default=36, help="decoder layers of the c4 model")
     ap.add_argument("--no-corr", action="store_true", help="mean correction off")
     ap.add_argument("--alpha", type=float, default=None)
+    ap.add_argument("--tile-q", type=int, default=None,
+                    help="query positions per selection tile (default: 128 packed rows = 128/G positions)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tiles", type=int, default=2048,
@@ -412,6 +424,8 @@ def main(argv=None) -> int:
     from tests.synthetic import topic_qkv
 
     base_cfg = fpv2.FPV2Config(alpha=alpha, mean_correction=not args.no_corr)
+    if args.tile_q is not None:
+        base_cfg = replace(base_cfg, tile_q=args.tile_q)
     cfg = _effective_config(base_cfg, Hq, Hkv)
     scale = D ** -0.5
 
@@ -620,7 +634,8 @@ def main(argv=None) -> int:
         peak_t = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
         dense_flops = 4.0 * D * Hq * length * (length + 1) / 2
         value = flops_layer / (ms_per_step * 1e-3) / 1e12
-        traffic = NCU_TRAFFIC_BYTES.get(args.config, {}) if world == 1 else {}
+        # (the committed ncu traffic figures are for the default tiles)
+        traffic = NCU_TRAFFIC_BYTES.get(args.config, {}) if world == 1 and args.tile_q is None else {}
         line = {
             "metric": METRIC,
             "value": round(value, 3),
@@ -638,7 +653,7 @@ def main(argv=None) -> int:
                 "workload": f"{args.config}: FPV2 layer L={length}, Hq={Hq}, Hkv={Hkv}, head_dim={D}, "
                             f"alpha={alpha}, correction={'on' if cfg.mean_correction else 'off'}, "
                             f"sink_tokens={cfg.sink_tokens}, window_tokens={cfg.window_tokens}, "
-                            f"last_n_blocks={cfg.last_n_blocks}, tile_q={cfg.tile_q} (128 packed rows)",
+                            f"last_n_blocks={cfg.last_n_blocks}, tile_q={cfg.tile_q} ({G * cfg.tile_q} packed rows)",
                 "parallelism": (f"head-parallel x{world}, output reassembled by NVLink multicast "
                                 "stores from the attention kernel" if mc is not None else
                                 f"head-parallel x{world} (+NCCL all-gather of the output)") if world > 1
@@ -660,7 +675,7 @@ def main(argv=None) -> int:
                 "selection_pct_hbm": round(100 * idx_gbs / peaks["hbm_gbs"], 2),
             },
             "roofline": {
-                "bound": "tensor", "kernel": "attn_tc_kernel (sparse attention)",
+                "bound": "tensor", "kernel": f"{attention_kernel_name(G, cfg.tile_q, D)} (sparse attention)",
                 "achieved": round(attn_tflops, 1), "peak": peak_t, "unit": "TFLOP/s",
                 "frac": round(attn_tflops / peak_t, 4), "traffic": traffic.get("attention"),
                 "traffic_unit": "bytes per launch (ncu, DRAM read + write)",

@@ -95,8 +95,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* v_full = k_empty + kStages;
   uint64_t* v_empty = v_full + kStages;
   uint64_t* s_full = v_empty + kStages;
-  uint64_t* s_free = s_full + kStages;
-  uint64_t* p_full = s_free + kStages;  // [kStages][2 half] (4 warps each)
+  uint64_t* p_full = s_full + kStages;  // [kStages][2 half] (4 warps each)
   uint64_t* pv_done = p_full + 2 * kStages;  // [1]
   uint64_t* o_full = pv_done + 1;        // [1]
   uint64_t* o_free = o_full + 1;         // [1]
@@ -125,7 +124,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&v_full[i]), 1);
       mbar_init(smem_u32(&v_empty[i]), 1);
       mbar_init(smem_u32(&s_full[i]), 1);
-      mbar_init(smem_u32(&s_free[i]), 1);
       mbar_init(smem_u32(&p_full[2 * i]), 4);
       mbar_init(smem_u32(&p_full[2 * i + 1]), 4);
     }
@@ -430,7 +428,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         first_pv = false;
         umma_commit(smem_u32(&v_empty[st]));
-        umma_commit(smem_u32(&s_free[st]));
         umma_commit(smem_u32(pv_done));
         return true;
       };
@@ -454,8 +451,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (rec.kind != KIND_EMPTY) {
           const int st = kv % kStages;
           const uint32_t par = (kv / kStages) & 1;
+          // S buffer st held P of item kv - 2, read by a PV issued earlier from
+          // this thread: tcgen05.mma ops run in issue order, so no wait here.
           ok = mbar_wait(smem_u32(&k_full[st]), par, wc);
-          if (ok) ok = mbar_wait(smem_u32(&s_free[st]), par ^ 1, wc);
           if (!ok) break;
           tc_fence_after();
           const uint32_t s_tmem = tmem_base + C::kSCol + st * 128;
@@ -802,7 +800,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int D>
 size_t smem_bytes() {
   return 1024 + (size_t)(2 + 2 * kStages) * Cfg<D>::kTileBytes + sizeof(Rec) * kRecs +
-         4 * kMaskWordsMax + 4 * (4 * 128 + 4 * 128) + 8 * (4 + 2 * kRecs + 8 * kStages + 10) + 16;
+         4 * kMaskWordsMax + 4 * (4 * 128 + 4 * 128) + 8 * (4 + 2 * kRecs + 7 * kStages + 10) + 16;
 }
 
 }  // namespace
@@ -826,7 +824,39 @@ bool attn_tc_supported(const AttnArgs& a) {
   return true;
 }
 
+// Tensor maps of one attention call: q, k, v, pooled k, pooled v, out.
+bool encode_attn_maps(const AttnArgs& a, CUtensorMap (&m)[6]) {
+  const int box_rows = a.tile_q >= 128 ? 128 : a.tile_q;
+  const int box_heads = 128 / box_rows;
+  if (!encode_tmap_3d(&m[0], a.q, a.dt, a.D, a.Lq_pad, a.Hq, 64, box_rows, box_heads))
+    return false;
+  // (with a multicast output the local tensor map is unused; q stands in for it)
+  if (!encode_tmap_3d(&m[5], a.out_mc != nullptr ? a.q : a.out, a.dt, a.D, a.Lq_pad, a.Hq, 64,
+                      box_rows, box_heads))
+    return false;
+  if (a.block_table != nullptr) {   // page pools [pages, page_size, Hkv, D]
+    const uint32_t rows = (uint32_t)std::min(a.page_size, 128);
+    if (!encode_tmap_pages(&m[1], a.k, a.dt, a.D, a.Hkv, a.page_size, a.num_pages, rows) ||
+        !encode_tmap_pages(&m[2], a.v, a.dt, a.D, a.Hkv, a.page_size, a.num_pages, rows))
+      return false;
+  } else {
+    if (!encode_tmap_3d(&m[1], a.k, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return false;
+    if (!encode_tmap_3d(&m[2], a.v, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return false;
+  }
+  // Pooled tiles (only read when pooled K/V share the compute dtype).
+  const bool pooled_ok = a.corr && a.pooled_dt == a.dt;
+  // (pooled tiles unused: q stands in for the pooled tensors)
+  if (!encode_tmap_3d(&m[3], pooled_ok ? a.pk : a.q, a.dt, a.D, pooled_ok ? a.Nb : a.Lq_pad,
+                      pooled_ok ? a.Hkv : a.Hq, 64, 128, 1))
+    return false;
+  if (!encode_tmap_3d(&m[4], pooled_ok ? a.pv : a.q, a.dt, a.D, pooled_ok ? a.Nb : a.Lq_pad,
+                      pooled_ok ? a.Hkv : a.Hq, 64, 128, 1))
+    return false;
+  return true;
+}
+
 cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, int* sched, cudaStream_t stream) {
+  if (attn_pair_supported(a)) return launch_attn_pair(a, L, sched, stream);
   Params p;
   p.a = a;
   p.nch = (a.G * a.tile_q) / 128;
@@ -839,33 +869,8 @@ cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, int* sched, cud
   p.budget = L.budget;
   if (p.items == 0) return cudaSuccess;
 
-  const int box_rows = a.tile_q >= 128 ? 128 : a.tile_q;
-  const int box_heads = 128 / box_rows;
-  CUtensorMap tq, tk, tv, tpk, tpv, to;
-  if (!encode_tmap_3d(&tq, a.q, a.dt, a.D, a.Lq_pad, a.Hq, 64, box_rows, box_heads))
-    return cudaErrorInvalidValue;
-  // (with a multicast output the local tensor map is unused; q stands in for it)
-  if (!encode_tmap_3d(&to, a.out_mc != nullptr ? a.q : a.out, a.dt, a.D, a.Lq_pad, a.Hq, 64,
-                      box_rows, box_heads))
-    return cudaErrorInvalidValue;
-  if (a.block_table != nullptr) {   // page pools [pages, page_size, Hkv, D]
-    const uint32_t rows = (uint32_t)std::min(a.page_size, 128);
-    if (!encode_tmap_pages(&tk, a.k, a.dt, a.D, a.Hkv, a.page_size, a.num_pages, rows) ||
-        !encode_tmap_pages(&tv, a.v, a.dt, a.D, a.Hkv, a.page_size, a.num_pages, rows))
-      return cudaErrorInvalidValue;
-  } else {
-    if (!encode_tmap_3d(&tk, a.k, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return cudaErrorInvalidValue;
-    if (!encode_tmap_3d(&tv, a.v, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return cudaErrorInvalidValue;
-  }
-  // Pooled tiles (only read when pooled K/V share the compute dtype).
-  const bool pooled_ok = a.corr && a.pooled_dt == a.dt;
-  // (pooled tiles unused: q stands in for the pooled tensors)
-  if (!encode_tmap_3d(&tpk, pooled_ok ? a.pk : a.q, a.dt, a.D, pooled_ok ? a.Nb : a.Lq_pad,
-                      pooled_ok ? a.Hkv : a.Hq, 64, 128, 1))
-    return cudaErrorInvalidValue;
-  if (!encode_tmap_3d(&tpv, pooled_ok ? a.pv : a.q, a.dt, a.D, pooled_ok ? a.Nb : a.Lq_pad,
-                      pooled_ok ? a.Hkv : a.Hq, 64, 128, 1))
-    return cudaErrorInvalidValue;
+  CUtensorMap m[6];
+  if (!encode_attn_maps(a, m)) return cudaErrorInvalidValue;
   const int grid = max(1, min(L.num_sms, p.items));
   cudaError_t e = cudaSuccess;
   if (sched != nullptr) {
@@ -878,7 +883,7 @@ cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, int* sched, cud
     e = cudaFuncSetAttribute(attn_tc_kernel<DD, TT>,                                        \
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
     if (e != cudaSuccess) return e;                                                         \
-    attn_tc_kernel<DD, TT><<<grid, kThreads, smem, stream>>>(tq, tk, tv, tpk, tpv, to, p);  \
+    attn_tc_kernel<DD, TT><<<grid, kThreads, smem, stream>>>(m[0], m[1], m[2], m[3], m[4], m[5], p);  \
   }
   if (a.D == 64 && a.dt == DT_BF16) FPV2_ATTN_LAUNCH(64, DT_BF16)
   else if (a.D == 64 && a.dt == DT_F16) FPV2_ATTN_LAUNCH(64, DT_F16)

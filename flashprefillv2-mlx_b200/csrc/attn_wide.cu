@@ -61,8 +61,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
   uint64_t* v_full = k_empty + 1;
   uint64_t* v_empty = v_full + 1;
   uint64_t* s_full = v_empty + 1;          // [2]
-  uint64_t* s_free = s_full + 2;           // [2]
-  uint64_t* p_full = s_free + 2;           // [2] (4 softmax warps)
+  uint64_t* p_full = s_full + 2;           // [2] (4 softmax warps)
   uint64_t* pv_done = p_full + 2;
   uint64_t* o_full = pv_done + 1;
   uint64_t* o_free = o_full + 1;           // 4 softmax warps
@@ -89,7 +88,6 @@ __global__ void __launch_bounds__(kWThreads, 1)
     mbar_init(smem_u32(v_empty), 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&s_full[i]), 1);
-      mbar_init(smem_u32(&s_free[i]), 1);
       mbar_init(smem_u32(&p_full[i]), 4);
     }
     mbar_init(smem_u32(pv_done), 1);
@@ -378,7 +376,6 @@ __global__ void __launch_bounds__(kWThreads, 1)
         }
         first_pv = false;
         umma_commit(smem_u32(v_empty));
-        umma_commit(smem_u32(&s_free[st]));
         umma_commit(smem_u32(pv_done));
         if (last) {
           umma_commit(smem_u32(o_full));
@@ -397,8 +394,9 @@ __global__ void __launch_bounds__(kWThreads, 1)
         if (rec.flags & 1) need_q = true;
         if (rec.kind != KIND_EMPTY) {
           const int st = kv & 1;
+          // S buffer st held P of item kv - 2, read by a PV issued earlier from
+          // this thread: tcgen05.mma ops run in issue order, so no wait here.
           ok = mbar_wait(smem_u32(k_full), kv & 1, wc);
-          if (ok) ok = mbar_wait(smem_u32(&s_free[st]), ((kv >> 1) & 1) ^ 1, wc);
           if (ok && need_q) {
             ok = mbar_wait(smem_u32(q_full), qcount & 1, wc);
             ++qcount;

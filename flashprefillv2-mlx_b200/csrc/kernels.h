@@ -119,6 +119,13 @@ cudaError_t launch_select_tc(const SelectTcArgs& a, const void* q, const void* p
 // counter; it is zeroed on `stream` before the launch. Null = static schedule.
 bool attn_tc_supported(const AttnArgs& a);
 cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, int* sched, cudaStream_t stream);
+// attn_pair.cu: the same with two query chunks of a tile per K/V stream;
+// launch_attn_tc routes the shapes it supports (an even number of chunks per
+// tile that pair up at the same query positions) to it.
+bool attn_pair_supported(const AttnArgs& a);
+cudaError_t launch_attn_pair(const AttnArgs& a, const TcLaunch& L, int* sched, cudaStream_t stream);
+// Tensor maps of one attention call (attn_tc.cu): q, k, v, pooled k, pooled v, out.
+bool encode_attn_maps(const AttnArgs& a, CUtensorMap (&m)[6]);
 // attn_wide.cu: the same for head_dim 256 (one softmax warp per row quarter).
 bool attn_wide_supported(const AttnArgs& a);
 cudaError_t launch_attn_wide(const AttnArgs& a, const TcLaunch& L, int* sched, cudaStream_t stream);

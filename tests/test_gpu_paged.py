@@ -9,6 +9,8 @@ kernels see the same tiles in the same order.
 
 from __future__ import annotations
 
+from dataclasses import replace
+
 import pytest
 import torch
 
@@ -31,20 +33,24 @@ def _pool(x: torch.Tensor, page_size: int, extra: int, seed: int):
     return cache, table
 
 
-@pytest.mark.parametrize("page_size,dtype,dim,offset", [
-    (16, torch.bfloat16, 128, 0),
-    (128, torch.bfloat16, 128, 0),
-    (256, torch.float16, 128, 0),
-    (32, torch.bfloat16, 96, 0),
-    (64, torch.bfloat16, 64, 0),
-    (16, torch.bfloat16, 128, 512),
+@pytest.mark.parametrize("page_size,dtype,dim,offset,tile_q", [
+    (16, torch.bfloat16, 128, 0, None),
+    (128, torch.bfloat16, 128, 0, None),
+    (256, torch.float16, 128, 0, None),
+    (32, torch.bfloat16, 96, 0, None),
+    (64, torch.bfloat16, 64, 0, None),
+    (16, torch.bfloat16, 128, 512, None),
+    (16, torch.bfloat16, 128, 0, 256),     # chunk pairs of a tile share K/V tiles
+    (64, torch.float16, 128, 512, 64),
 ])
-def test_paged_attention_equals_contiguous(page_size, dtype, dim, offset):
+def test_paged_attention_equals_contiguous(page_size, dtype, dim, offset, tile_q):
     length, hq, hkv = 2048, 8, 2
     q, k, v = topic_qkv(length=length, query_heads=hq, kv_heads=hkv, head_dim=dim, seed=5, dtype=dtype)
     q = q[:, offset:].contiguous()
     ql = length - offset
     cfg = _effective_config(fpv2.FPV2Config(alpha=0.1, sink_tokens=128, window_tokens=256), hq, hkv)
+    if tile_q is not None:
+        cfg = replace(cfg, tile_q=tile_q)
     scale = dim ** -0.5
     qg, kg, vg = q.to(DEV), k.to(DEV), v.to(DEV)
     pk, pv, lists, _ = fpv2.index_stage(qg, kg, vg, scale=scale, config=cfg, offset=offset,

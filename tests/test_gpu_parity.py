@@ -275,7 +275,13 @@ ATTN_CASES = [
     (128, torch.float16, True, 0.1, None),
     (64, torch.bfloat16, True, 0.15, None),
     (128, torch.bfloat16, True, 0.0, None),
-    (128, torch.bfloat16, True, 0.15, 128),   # direct 128-position tiles: 4 chunks per tile
+    (128, torch.bfloat16, True, 0.15, 128),   # direct 128-position tiles: 4 chunks per tile (pairs)
+    (128, torch.float16, True, 0.1, 128),
+    (128, torch.bfloat16, False, 0.0, 128),
+    (64, torch.bfloat16, True, 0.15, 128),
+    (96, torch.bfloat16, True, 0.15, 128),
+    (128, torch.bfloat16, True, 0.15, 64),    # 2 chunks of 2 heads x 64 positions (pair)
+    (128, torch.bfloat16, True, 0.15, 256),   # 8 chunks: pairs of heads at each position slice
     (96, torch.bfloat16, True, 0.15, None),   # tensor cores on zero-padded 128-wide tiles
     (96, torch.float16, False, 0.1, None),
     (256, torch.bfloat16, True, 0.15, None),  # attn_wide_kernel
