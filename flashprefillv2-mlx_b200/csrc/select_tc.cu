@@ -105,13 +105,20 @@ __device__ __forceinline__ float lg2(float x) {
   return y;
 }
 
+// Bits [0, n) of a 32-bit word (n clamped to [0, 32]).
+__device__ __forceinline__ uint32_t prefix_bits(long long n) {
+  return n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
 
-template <int D>
+// kContig: each query chunk holds consecutive positions of one head (tile_q a
+// multiple of the chunk width), so element masks are column ranges.
+template <int D, bool kContig>
 __global__ void __launch_bounds__(kThreads, 1)
     select_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                      const __grid_constant__ CUtensorMap tmap_k, Params p) {
@@ -180,6 +187,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   WaitCtx wc{p.status, abort_flag, p.budget};
   const int total_work = g.Hkv * g.Nt;
+  // Tiles of several query chunks: the producer and the issuer walk two items
+  // (one per energy group) together, alternating their score tiles, so both
+  // groups stay busy. (A 256-wide Q chunk has a single stage: one item at a time.)
+  const int npair = (C::kQStages >= 2 && p.n_chunks > 1) ? 2 : 1;
 
   if (warp == 0) {
     // ======================= TMA producer =================================
@@ -190,38 +201,96 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < C::kKStagesMax; ++i) { kuse[i] = 0; ktag[i] = -1; }
       bool ok = true;
-      for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x) {
-        const Item it = make_item(p, w);
-        if (it.n_mt == 0) continue;
-        for (int c = 0; c < p.n_chunks && ok; ++c) {
-          const int qs = qcount % C::kQStages;
-          ok = mbar_wait(smem_u32(&q_empty[qs]), ((qcount / C::kQStages) & 1) ^ 1, wc);
-          if (!ok) break;
-          ++qcount;
-          const uint32_t qb = smem_u32(&q_full[qs]);
-          mbar_arrive_expect_tx(qb, (uint32_t)(p.NC * D * 2));
-          const int P0 = c * p.NC;
-          const int g0 = P0 / g.tile_q, p0 = P0 % g.tile_q;
-#pragma unroll
-          for (int hh = 0; hh < C::kHalves; ++hh)
-            tma_load_3d(q_smem + qs * C::kQBytes + hh * p.NC * 128, &tmap_q, qb, hh * 64,
-                        it.t * g.tile_q + p0, it.h * g.G + g0);
-          for (int m = 0; m < it.n_mt; ++m) {
-            const int s = m % KS;
-            ok = mbar_wait(smem_u32(&k_empty[s]), (kuse[s] & 1) ^ 1, wc);
+      if (npair == 1) {
+        for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x) {
+          const Item it = make_item(p, w);
+          if (it.n_mt == 0) continue;
+          for (int c = 0; c < p.n_chunks && ok; ++c) {
+            const int qs = qcount % C::kQStages;
+            ok = mbar_wait(smem_u32(&q_empty[qs]), ((qcount / C::kQStages) & 1) ^ 1, wc);
             if (!ok) break;
-            ++kuse[s];
-            const int tag = it.h * 4096 + m;
-            const uint32_t kb = smem_u32(&k_full[s]);
-            if (ktag[s] == tag) {
-              mbar_arrive(kb);   // tile still resident
-            } else {
-              ktag[s] = tag;
-              mbar_arrive_expect_tx(kb, (uint32_t)(128 * D * 2));
-#pragma unroll
+            ++qcount;
+            const uint32_t qb = smem_u32(&q_full[qs]);
+            mbar_arrive_expect_tx(qb, (uint32_t)(p.NC * D * 2));
+            const int P0 = c * p.NC;
+            const int g0 = P0 / g.tile_q, p0 = P0 % g.tile_q;
+  #pragma unroll
+            for (int hh = 0; hh < C::kHalves; ++hh)
+              tma_load_3d(q_smem + qs * C::kQBytes + hh * p.NC * 128, &tmap_q, qb, hh * 64,
+                          it.t * g.tile_q + p0, it.h * g.G + g0);
+            for (int m = 0; m < it.n_mt; ++m) {
+              const int s = m % KS;
+              ok = mbar_wait(smem_u32(&k_empty[s]), (kuse[s] & 1) ^ 1, wc);
+              if (!ok) break;
+              ++kuse[s];
+              const int tag = it.h * 4096 + m;
+              const uint32_t kb = smem_u32(&k_full[s]);
+              if (ktag[s] == tag) {
+                mbar_arrive(kb);   // tile still resident
+              } else {
+                ktag[s] = tag;
+                mbar_arrive_expect_tx(kb, (uint32_t)(128 * D * 2));
+  #pragma unroll
+                for (int hh = 0; hh < C::kHalves; ++hh)
+                  tma_load_3d(k_smem + s * C::kKBytes + hh * 128 * 128, &tmap_k, kb, hh * 64, m * 128,
+                              it.h);
+              }
+            }
+          }
+        }
+      } else {
+        for (int w = blockIdx.x; w < total_work && ok; w += npair * gridDim.x) {
+          Item its[2];
+          int nmt[2] = {0, 0}, nmax = 0;
+  #pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            const int wx = w + x * gridDim.x;
+            if (x < npair && wx < total_work) {
+              its[x] = make_item(p, wx);
+              nmt[x] = its[x].n_mt;
+            }
+            nmax = max(nmax, nmt[x]);
+          }
+          if (nmax == 0) continue;
+          for (int c = 0; c < p.n_chunks && ok; ++c) {
+  #pragma unroll
+            for (int x = 0; x < 2; ++x) {
+              if (nmt[x] == 0 || !ok) continue;
+              const Item& it = its[x];
+              const int qs = qcount % C::kQStages;
+              ok = mbar_wait(smem_u32(&q_empty[qs]), ((qcount / C::kQStages) & 1) ^ 1, wc);
+              if (!ok) break;
+              ++qcount;
+              const uint32_t qb = smem_u32(&q_full[qs]);
+              mbar_arrive_expect_tx(qb, (uint32_t)(p.NC * D * 2));
+              const int P0 = c * p.NC;
+              const int g0 = P0 / g.tile_q, p0 = P0 % g.tile_q;
+  #pragma unroll
               for (int hh = 0; hh < C::kHalves; ++hh)
-                tma_load_3d(k_smem + s * C::kKBytes + hh * 128 * 128, &tmap_k, kb, hh * 64, m * 128,
-                            it.h);
+                tma_load_3d(q_smem + qs * C::kQBytes + hh * p.NC * 128, &tmap_q, qb, hh * 64,
+                            it.t * g.tile_q + p0, it.h * g.G + g0);
+            }
+            for (int m = 0; m < nmax && ok; ++m) {
+  #pragma unroll
+              for (int x = 0; x < 2; ++x) {
+                if (m >= nmt[x] || !ok) continue;
+                const int s = m % KS;
+                ok = mbar_wait(smem_u32(&k_empty[s]), (kuse[s] & 1) ^ 1, wc);
+                if (!ok) break;
+                ++kuse[s];
+                const int tag = its[x].h * 4096 + m;
+                const uint32_t kb = smem_u32(&k_full[s]);
+                if (ktag[s] == tag) {
+                  mbar_arrive(kb);   // tile still resident
+                } else {
+                  ktag[s] = tag;
+                  mbar_arrive_expect_tx(kb, (uint32_t)(128 * D * 2));
+  #pragma unroll
+                  for (int hh = 0; hh < C::kHalves; ++hh)
+                    tma_load_3d(k_smem + s * C::kKBytes + hh * 128 * 128, &tmap_k, kb, hh * 64, m * 128,
+                                its[x].h);
+                }
+              }
             }
           }
         }
@@ -245,40 +314,94 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < C::kKStagesMax; ++i) kuse[i] = 0;
       bool ok = true;
       int j = 0;   // CTA-local item index: item j belongs to energy group j % kGroups
-      for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x, ++j) {
-        const Item it = make_item(p, w);
-        if (it.n_mt == 0) continue;
-        const int grp = j % kGroups;
-        for (int c = 0; c < p.n_chunks && ok; ++c) {
-          const int qs = qcount % C::kQStages;
-          ok = mbar_wait(smem_u32(&q_full[qs]), (qcount / C::kQStages) & 1, wc);
-          if (!ok) break;
-          ++qcount;
-          for (int m = 0; m < it.n_mt; ++m) {
-            const int s = m % KS;
-            ok = mbar_wait(smem_u32(&k_full[s]), kuse[s] & 1, wc);
+      if (npair == 1) {
+        for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x, ++j) {
+          const Item it = make_item(p, w);
+          if (it.n_mt == 0) continue;
+          const int grp = j % kGroups;
+          for (int c = 0; c < p.n_chunks && ok; ++c) {
+            const int qs = qcount % C::kQStages;
+            ok = mbar_wait(smem_u32(&q_full[qs]), (qcount / C::kQStages) & 1, wc);
             if (!ok) break;
-            ++kuse[s];
-            const int tc = tcount[grp];
-            const int ts = grp * kSlotsPerGroup + tc % kSlotsPerGroup;
-            ok = mbar_wait(smem_u32(&t_empty[ts]), ((tc / kSlotsPerGroup) & 1) ^ 1, wc);
-            if (!ok) break;
-            ++tcount[grp];
-            tc_fence_after();
-            const uint32_t d_tmem = tmem_base + ts * 128;
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const int hh = kk / 4, sub = kk % 4;
-              const uint64_t a_desc =
-                  sw128_desc(k_smem + s * C::kKBytes + hh * 128 * 128 + sub * 32, 16, 1024);
-              const uint64_t b_desc =
-                  sw128_desc(q_smem + qs * C::kQBytes + hh * p.NC * 128 + sub * 32, 16, 1024);
-              umma_ss(d_tmem, a_desc, b_desc, p.idesc, kk > 0 ? 1u : 0u);
+            ++qcount;
+            for (int m = 0; m < it.n_mt; ++m) {
+              const int s = m % KS;
+              ok = mbar_wait(smem_u32(&k_full[s]), kuse[s] & 1, wc);
+              if (!ok) break;
+              ++kuse[s];
+              const int tc = tcount[grp];
+              const int ts = grp * kSlotsPerGroup + tc % kSlotsPerGroup;
+              ok = mbar_wait(smem_u32(&t_empty[ts]), ((tc / kSlotsPerGroup) & 1) ^ 1, wc);
+              if (!ok) break;
+              ++tcount[grp];
+              tc_fence_after();
+              const uint32_t d_tmem = tmem_base + ts * 128;
+  #pragma unroll
+              for (int kk = 0; kk < D / 16; ++kk) {
+                const int hh = kk / 4, sub = kk % 4;
+                const uint64_t a_desc =
+                    sw128_desc(k_smem + s * C::kKBytes + hh * 128 * 128 + sub * 32, 16, 1024);
+                const uint64_t b_desc =
+                    sw128_desc(q_smem + qs * C::kQBytes + hh * p.NC * 128 + sub * 32, 16, 1024);
+                umma_ss(d_tmem, a_desc, b_desc, p.idesc, kk > 0 ? 1u : 0u);
+              }
+              umma_commit(smem_u32(&t_full[ts]));
+              umma_commit(smem_u32(&k_empty[s]));
             }
-            umma_commit(smem_u32(&t_full[ts]));
-            umma_commit(smem_u32(&k_empty[s]));
+            if (ok) umma_commit(smem_u32(&q_empty[qs]));
           }
-          if (ok) umma_commit(smem_u32(&q_empty[qs]));
+        }
+      } else {
+        for (int w = blockIdx.x; w < total_work && ok; w += npair * gridDim.x, j += npair) {
+          int nmt[2] = {0, 0}, nmax = 0;
+  #pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            const int wx = w + x * gridDim.x;
+            if (x < npair && wx < total_work) nmt[x] = make_item(p, wx).n_mt;
+            nmax = max(nmax, nmt[x]);
+          }
+          if (nmax == 0) continue;
+          for (int c = 0; c < p.n_chunks && ok; ++c) {
+            int qsx[2] = {0, 0};
+  #pragma unroll
+            for (int x = 0; x < 2; ++x) {
+              if (nmt[x] == 0 || !ok) continue;
+              qsx[x] = qcount % C::kQStages;
+              ok = mbar_wait(smem_u32(&q_full[qsx[x]]), (qcount / C::kQStages) & 1, wc);
+              ++qcount;
+            }
+            for (int m = 0; m < nmax && ok; ++m) {
+  #pragma unroll
+              for (int x = 0; x < 2; ++x) {
+                if (m >= nmt[x] || !ok) continue;
+                const int grp = (j + x) % kGroups;
+                const int s = m % KS;
+                ok = mbar_wait(smem_u32(&k_full[s]), kuse[s] & 1, wc);
+                if (!ok) break;
+                ++kuse[s];
+                const int tc = tcount[grp];
+                const int ts = grp * kSlotsPerGroup + tc % kSlotsPerGroup;
+                ok = mbar_wait(smem_u32(&t_empty[ts]), ((tc / kSlotsPerGroup) & 1) ^ 1, wc);
+                if (!ok) break;
+                ++tcount[grp];
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + ts * 128;
+                const uint32_t qsm = q_smem + qsx[x] * C::kQBytes;
+  #pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                  const int hh = kk / 4, sub = kk % 4;
+                  const uint64_t a_desc =
+                      sw128_desc(k_smem + s * C::kKBytes + hh * 128 * 128 + sub * 32, 16, 1024);
+                  const uint64_t b_desc = sw128_desc(qsm + hh * p.NC * 128 + sub * 32, 16, 1024);
+                  umma_ss(d_tmem, a_desc, b_desc, p.idesc, kk > 0 ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&t_full[ts]));
+                umma_commit(smem_u32(&k_empty[s]));
+                // this item's query chunk is read for the last time
+                if (m == nmt[x] - 1) umma_commit(smem_u32(&q_empty[qsx[x]]));
+              }
+            }
+          }
         }
       }
       // Drain: every MMA issued by this thread has completed once `drain` flips.
@@ -351,7 +474,21 @@ __global__ void __launch_bounds__(kThreads, 1)
               reg_fence(sv[0]);
               reg_fence(sv[1]);
               uint32_t vm[2] = {0xffffffffu, 0xffffffffu};
-              if (masked) {
+              if (kContig && masked) {
+                // The chunk's columns are consecutive positions row0 + col: the
+                // visible columns of block b form the range [lo, hi).
+                const long long row0 = (long long)it.t * g.tile_q + (cc * p.NC) % g.tile_q;
+                long long lo = 0, hi = p.NC;
+                if (it.row_mask) {
+                  lo = max(lo, bstart - g.offset - row0);            // bstart <= offset + row
+                  hi = min(hi, (long long)g.valid_lq - row0);         // row < valid_lq
+                }
+#pragma unroll
+                for (int q2 = 0; q2 < 2; ++q2) {
+                  const long long c0 = hf * 64 + q2 * 32;
+                  vm[q2] = prefix_bits(hi - c0) & ~prefix_bits(lo - c0);
+                }
+              } else if (masked) {
 #pragma unroll 1
                 for (int q2 = 0; q2 < 2; ++q2) {
                   uint32_t bits = 0u;
@@ -591,29 +728,21 @@ cudaError_t launch_select_tc(const SelectTcArgs& a, const void* q, const void* p
     grid = L.num_sms;
   }
   grid = max(1, min(grid, total));
+  const bool contig = g.tile_q % a.NC == 0;
   cudaError_t e;
-  if (g.D == 64) {
-    p.k_stages = pick_k_stages<64>(g.Nb);
-    const size_t smem = smem_bytes<64>(g.Nb, p.k_stages);
-    e = cudaFuncSetAttribute(select_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
-    if (e != cudaSuccess) return e;
-    select_tc_kernel<64><<<grid, kThreads, smem, stream>>>(tq, tk, p);
-  } else if (g.D == 256) {
-    p.k_stages = pick_k_stages<256>(g.Nb);
-    const size_t smem = smem_bytes<256>(g.Nb, p.k_stages);
-    e = cudaFuncSetAttribute(select_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
-    if (e != cudaSuccess) return e;
-    select_tc_kernel<256><<<grid, kThreads, smem, stream>>>(tq, tk, p);
-  } else {
-    p.k_stages = pick_k_stages<128>(g.Nb);
-    const size_t smem = smem_bytes<128>(g.Nb, p.k_stages);
-    e = cudaFuncSetAttribute(select_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
-    if (e != cudaSuccess) return e;
-    select_tc_kernel<128><<<grid, kThreads, smem, stream>>>(tq, tk, p);
+#define FPV2_SELECT_LAUNCH(DD)                                                                 \
+  {                                                                                            \
+    p.k_stages = pick_k_stages<DD>(g.Nb);                                                      \
+    const size_t smem = smem_bytes<DD>(g.Nb, p.k_stages);                                      \
+    auto kern = contig ? select_tc_kernel<DD, true> : select_tc_kernel<DD, false>;             \
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
+    if (e != cudaSuccess) return e;                                                            \
+    kern<<<grid, kThreads, smem, stream>>>(tq, tk, p);                                         \
   }
+  if (g.D == 64) FPV2_SELECT_LAUNCH(64)
+  else if (g.D == 256) FPV2_SELECT_LAUNCH(256)
+  else FPV2_SELECT_LAUNCH(128)
+#undef FPV2_SELECT_LAUNCH
   return cudaGetLastError();
 }
 

@@ -94,7 +94,7 @@ def test_alpha_zero_lower_triangle_on_gpu(dtype):
 # ---------------------------------------------------------------------------
 
 SELECT_CASES = [
-    # length, Hq, Hkv, D, dtype, alpha, seed
+    # length, Hq, Hkv, D, dtype, alpha, seed[, tile_q (default: 128 packed rows)]
     (2048, 8, 2, 128, torch.bfloat16, 0.1, 0),
     (2048, 8, 2, 128, torch.float16, 0.15, 1),
     (4096, 32, 8, 128, torch.bfloat16, 0.1, 2),
@@ -104,15 +104,23 @@ SELECT_CASES = [
     (2048, 8, 2, 256, torch.bfloat16, 0.1, 6),      # 256-wide chunks, single-buffered Q
     (2048, 8, 2, 48, torch.bfloat16, 0.1, 7),       # generic CUDA-core path
     (1024, 8, 2, 128, torch.float32, 0.1, 6),       # generic, fp32
+    (2048, 8, 2, 128, torch.bfloat16, 0.1, 8, 256),   # 8 query chunks per tile: two items interleaved
+    (4096, 8, 2, 128, torch.float16, 0.15, 9, 128),
+    (2048, 8, 2, 64, torch.bfloat16, 0.1, 10, 64),
+    (2048, 8, 2, 256, torch.bfloat16, 0.1, 11, 128),  # 256-wide chunks: one item at a time
 ]
 
 
-@pytest.mark.parametrize("case", SELECT_CASES, ids=lambda c: f"L{c[0]}-Hq{c[1]}-D{c[3]}-{c[4]}")
+@pytest.mark.parametrize("case", SELECT_CASES,
+                         ids=lambda c: f"L{c[0]}-Hq{c[1]}-D{c[3]}-{c[4]}" + (f"-t{c[7]}" if len(c) > 7 else ""))
 def test_selection_parity(case):
-    length, hq, hkv, d, dtype, alpha, seed = case
+    length, hq, hkv, d, dtype, alpha, seed = case[:7]
+    tile_q = case[7] if len(case) > 7 else None
     q, k, v = topic_qkv(length=length, query_heads=hq, kv_heads=hkv, head_dim=d, seed=seed,
                         dtype=dtype)
     cfg = _effective_config(fpv2.FPV2Config(alpha=alpha, score_chunk_tiles=8), hq, hkv)
+    if tile_q is not None:
+        cfg = replace(cfg, tile_q=tile_q)
     qg, kg = cuda(q, k)
     pk = fpv2.pool_blocks(kg, 128)
     pk_ref = O.pool_blocks(P.np32(k), 128, P.dtname(dtype))
