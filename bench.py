@@ -96,14 +96,17 @@ def retained_attention_flops(sel_ids, sel_counts, pr_counts, *, G, tile_q, block
     return 4.0 * D * total
 
 
-def attention_kernel_name(G: int, tile_q: int, D: int) -> str:
-    """The tensor-core attention kernel the library picks for this tile shape
-    (csrc/attn_pair.cu: chunks of a tile that pair up at the same positions)."""
+def attention_kernel_name(dtype, Hq: int, Hkv: int, D: int, block_k: int, tile_q: int,
+                          num_blocks: int) -> str:
+    """The attention kernel the library picks for this shape (fpv2_fast_path_mask)."""
+    from fpv2 import _lib
+
+    m = _lib.fast_path_mask(dtype, Hq, Hkv, D, block_k, tile_q, num_blocks)
+    if not m & 2:
+        return "attn_generic_kernel"
     if D == 256:
         return "attn_wide_kernel"
-    nch = G * tile_q // 128
-    per_group = tile_q // 128 if tile_q >= 128 else 1
-    return "attn_pair_kernel" if nch >= 2 and (nch // per_group) % 2 == 0 else "attn_tc_kernel"
+    return "attn_pair_kernel" if m & 4 else "attn_tc_kernel"
 
 
 def index_stage_bytes(Hq, Hkv, L, D, Nt, Nb, esize=2) -> int:
@@ -675,7 +678,7 @@ def main(argv=None) -> int:
                 "selection_pct_hbm": round(100 * idx_gbs / peaks["hbm_gbs"], 2),
             },
             "roofline": {
-                "bound": "tensor", "kernel": f"{attention_kernel_name(G, cfg.tile_q, D)} (sparse attention)",
+                "bound": "tensor", "kernel": f"{attention_kernel_name(dtype, Hq, Hkv, D, cfg.block_k, cfg.tile_q, length // cfg.block_k)} (sparse attention)",
                 "achieved": round(attn_tflops, 1), "peak": peak_t, "unit": "TFLOP/s",
                 "frac": round(attn_tflops / peak_t, 4), "traffic": traffic.get("attention"),
                 "traffic_unit": "bytes per launch (ncu, DRAM read + write)",

@@ -643,6 +643,7 @@ int fpv2_fast_path_mask(int dtype, int32_t q_heads, int32_t kv_heads, int32_t he
   int m = 0;
   if (select_tc_supported(g, dtype)) m |= 1;
   if (attn_tc_supported(a) || attn_wide_supported(a)) m |= 2;
+  if (attn_pair_supported(a)) m |= 4;
   return m;
 }
 

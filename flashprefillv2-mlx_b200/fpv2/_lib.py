@@ -196,6 +196,7 @@ def set_wait_budget_ms(milliseconds: float) -> None:
 
 def fast_path_mask(dtype: torch.dtype, q_heads: int, kv_heads: int, head_dim: int,
                    block_k: int, tile_q: int, num_blocks: int) -> int:
-    """Bit 0: tcgen05 index stage; bit 1: tcgen05 attention for this shape."""
+    """Bit 0: tcgen05 index stage; bit 1: tcgen05 attention for this shape;
+    bit 2: the attention pairs two chunks of a selection tile per K/V stream."""
     return int(lib().fpv2_fast_path_mask(dtype_code(dtype), q_heads, kv_heads, head_dim,
                                          block_k, tile_q, num_blocks))

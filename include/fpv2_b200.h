@@ -235,7 +235,9 @@ FPV2_API int fpv2_pool_pages(const void* pages, const int32_t* block_table, int3
 /*
  * Which kernel family the two stages would use for this shape:
  * bit 0 set = tcgen05 index stage, bit 1 set = tcgen05 attention
- * (otherwise the generic CUDA-core kernels run).
+ * (otherwise the generic CUDA-core kernels run), bit 2 set = the attention
+ * takes two 128-row chunks of a selection tile per K/V stream (tiles of
+ * several chunks at the same query positions).
  */
 FPV2_API int fpv2_fast_path_mask(int dtype, int32_t q_heads, int32_t kv_heads, int32_t head_dim,
                         int32_t block_k, int32_t tile_q, int32_t num_blocks);

@@ -40,7 +40,9 @@ def test_library_exports_every_declared_symbol():
 def test_fast_path_selection_rules_without_gpu():
     assert _lib.fast_path_mask(torch.bfloat16, 32, 8, 128, 128, 32, 512) == 3
     assert _lib.fast_path_mask(torch.float16, 64, 8, 128, 128, 16, 1024) == 3
-    assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 128, 128, 128, 16) == 3   # direct tile_q 128
+    assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 128, 128, 128, 16) == 7   # direct tile_q 128: chunk pairs
+    assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 64, 128, 64, 16) == 7     # 2 chunks of 2 heads x 64
+    assert _lib.fast_path_mask(torch.bfloat16, 2, 2, 128, 128, 256, 16) == 3   # one head: slices differ in position
     assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 96, 128, 32, 16) == 3   # zero-padded 128-wide tiles
     assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 256, 128, 32, 16) == 3
     assert _lib.fast_path_mask(torch.bfloat16, 8, 2, 48, 128, 32, 16) == 0
