@@ -43,9 +43,9 @@ METRIC = "sparse prefill-attn ms/layer & TFLOP/s (retained) at 64k; % bf16 peak;
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
-# DRAM bytes per launch of the dominant kernels, from one ncu capture of the
-# full-size single-GPU workload (dram__bytes_read.sum + dram__bytes_write.sum;
-# profiles/dram_traffic_c3.md has the command and the per-kernel split).
+# DRAM bytes per launch of the dominant kernels (dram__bytes_read.sum +
+# dram__bytes_write.sum) from one earlier ncu capture of the full-size
+# single-GPU workload: a recorded constant, not measured by this run.
 NCU_TRAFFIC_BYTES = {
     "c3": {"attention": 2890.32e6 + 501.88e6, "index_stage": 268.45e6 + 1.33e6 + 537.55e6 + 57.75e6},
 }
@@ -179,10 +179,12 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 
 
-def cpu_sample(q, k, v, cfg, *, tiles_per_step: int, head: int = 0, seed_tile: int | None = None):
-    """Run the oracle's index stage + blockwise attention for ``tiles_per_step``
+def cpu_sample(q, k, v, cfg, *, tiles_per_step: int, head: int = 0, seed_tile: int | None = None,
+               want_outputs: bool = False):
+    """Run the oracle's index stage + list-driven attention for ``tiles_per_step``
     tiles of KV head ``head`` (latest tiles, the heaviest) and return
-    (seconds, retained FLOPs, description)."""
+    (seconds, retained FLOPs, description) -- plus, with ``want_outputs``, the
+    oracle's lists and float32 output of those tiles for the parity check."""
     from oracle import fpv2_oracle as O
 
     hq, L, D = q.shape
@@ -194,9 +196,10 @@ def cpu_sample(q, k, v, cfg, *, tiles_per_step: int, head: int = 0, seed_tile: i
     qh = q[head * G:(head + 1) * G].float().numpy()
     kh = k[head:head + 1].float().numpy()
     vh = v[head:head + 1].float().numpy()
+    pdt = "fp16" if q.dtype == torch.float16 else "bf16"
     t0 = time.perf_counter()
-    pk = O.pool_blocks(kh, cfg.block_k, "bf16")
-    pv = O.pool_blocks(vh, cfg.block_k, "bf16")
+    pk = O.pool_blocks(kh, cfg.block_k, pdt)
+    pv = O.pool_blocks(vh, cfg.block_k, pdt)
     # selection for the sampled tiles only: slice their rows (offset keeps positions)
     row0 = tiles[0] * cfg.tile_q
     rows = slice(row0, (tiles[-1] + 1) * cfg.tile_q)
@@ -206,7 +209,7 @@ def cpu_sample(q, k, v, cfg, *, tiles_per_step: int, head: int = 0, seed_tile: i
     lists = O.compact_block_indices(sel, config=c, offset=row0, query_length=qh[:, rows].shape[1],
                                     key_length=L)
     out = O.sparse_attention(qh[:, rows], kh, vh, pk, pv, *lists, scale=D ** -0.5, config=c,
-                             offset=row0, dtype="bf16")
+                             offset=row0, dtype=pdt, out_dtype="fp32")
     dt = time.perf_counter() - t0
     assert np.isfinite(out).all()
     flops = retained_attention_flops(torch.from_numpy(lists[0]), torch.from_numpy(lists[1]),
@@ -217,7 +220,40 @@ def cpu_sample(q, k, v, cfg, *, tiles_per_step: int, head: int = 0, seed_tile: i
     desc = (f"KV head {head}, tiles {tiles[0]}..{tiles[-1]} ({len(tiles)} of {nt} per head, "
             f"{len(tiles) * G * cfg.tile_q} query rows): oracle pool + select + compact + "
             f"list-driven attention, numpy float32")
-    return dt, flops, desc
+    if not want_outputs:
+        return dt, flops, desc
+    return dt, flops, desc, dict(head=head, row0=row0, tiles=tiles, lists=lists, out=out)
+
+
+def sample_parity(samples, lists_gpu, out_gpu, G: int, tile_q: int) -> dict:
+    """GPU lists and output of the CPU sample's tiles vs the oracle's: full-width
+    lists bit-exact per tile (an in-band threshold flip shows as a mismatched
+    tile) and the output within max-abs 2e-2 / mean-abs 2e-3 of the float32
+    list-driven math (outside the timed region)."""
+    tiles_total = mismatched = 0
+    mx, sum_abs, n = 0.0, 0.0, 0
+    for smp in samples:
+        h, tiles = smp["head"], smp["tiles"]
+        t0, t1 = tiles[0], tiles[-1] + 1
+        gpu_lists = [x[h:h + 1, t0:t1].cpu().numpy() for x in lists_gpu]
+        equal = np.ones(t1 - t0, dtype=bool)
+        for got, exp in zip(gpu_lists, smp["lists"]):
+            same = (got == exp).reshape(t1 - t0, -1).all(axis=1)
+            equal &= same
+        tiles_total += t1 - t0
+        mismatched += int((~equal).sum())
+        r0, r1 = t0 * tile_q, t1 * tile_q
+        o = out_gpu[h * G:(h + 1) * G, r0:r1].to("cpu", torch.float32).numpy()
+        err = np.abs(o - smp["out"][:, :r1 - r0])
+        mx = max(mx, float(err.max()))
+        sum_abs += float(err.sum())
+        n += err.size
+    mean = sum_abs / max(n, 1)
+    return {"tiles_checked": tiles_total, "tiles_with_list_mismatch": mismatched,
+            "max_abs": round(mx, 6), "mean_abs": round(mean, 7),
+            "ok": bool(mismatched == 0 and mx <= 2e-2 and mean <= 2e-3),
+            "criterion": "full-width lists bit-exact per tile; output max-abs <= 2e-2 and mean-abs "
+                         "<= 2e-3 against the oracle's float32 list-driven math on the same tiles"}
 
 
 # ---------------------------------------------------------------------------
@@ -615,18 +651,29 @@ def main(argv=None) -> int:
                "ms_per_layer": round(e2e_ms, 3), "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h)}
 
-    # ---- CPU baseline (rank 0, N = 1 only) ----
+    # ---- CPU baseline (rank 0, N = 1 only), and the parity of its sample ----
     cpu = None
+    parity = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # one more (untimed) layer on the device, kept for the parity check
+        pk_p, pv_p, lists_p, _ = fpv2.index_stage(qd[0], kd[0], vd[0], scale=scale, config=cfg,
+                                                  offset=0, query_length=length, key_length=length)
+        out_p = fpv2.sparse_attention(qd[0], kd[0], vd[0], pk_p, pv_p, *lists_p, scale=scale,
+                                      config=cfg)
+        torch.cuda.synchronize()
         torch.set_num_threads(os.cpu_count() or 1)
-        dt, fl, descs = 0.0, 0.0, []
+        dt, fl, descs, samples = 0.0, 0.0, [], []
         for head in range(min(args.cpu_heads, Hkv)):   # about 10 s of host work by default
-            d_h, f_h, desc_h = cpu_sample(q, k, v, cfg, tiles_per_step=args.cpu_tiles, head=head)
+            d_h, f_h, desc_h, smp = cpu_sample(q, k, v, cfg, tiles_per_step=args.cpu_tiles,
+                                               head=head, want_outputs=True)
             dt += d_h
             fl += f_h
             descs.append(desc_h)
+            samples.append(smp)
         cpu = {"value": round(fl / dt / 1e12, 6), "unit": "TFLOP/s", "cores": os.cpu_count(),
                "kind": "port", "sample": "; ".join(descs), "seconds": round(dt, 2)}
+        parity = sample_parity(samples, lists_p, out_p, G, cfg.tile_q)
+        del pk_p, pv_p, lists_p, out_p
 
     if rank == 0:
         peaks, peak_src = load_peaks()
@@ -634,7 +681,9 @@ def main(argv=None) -> int:
         idx_bytes_rank = index_stage_bytes(hkv_r * G, hkv_r, length, D, nt_all, nb_all)
         attn_tflops = flops_rank / (attn_ms * 1e-3) / 1e12
         idx_gbs = idx_bytes_rank / (idx_ms * 1e-3) / 1e9
-        peak_t = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+        # the timed region is tens of milliseconds, not a seconds-long loop: burst peak
+        peak_t = peaks["bf16_tflops"]
+        peak_sus = peaks.get("bf16_tflops_sustained", peak_t)
         dense_flops = 4.0 * D * Hq * length * (length + 1) / 2
         value = flops_layer / (ms_per_step * 1e-3) / 1e12
         # (the committed ncu traffic figures are for the default tiles)
@@ -674,6 +723,7 @@ def main(argv=None) -> int:
                 "selection_gbs": round(idx_gbs, 1),
                 "attention_tflops": round(attn_tflops, 1),
                 "attention_pct_bf16_peak": round(100 * attn_tflops / peak_t, 2),
+                "attention_pct_bf16_sustained": round(100 * attn_tflops / peak_sus, 2),
                 "attention_pct_bf16_spec_2250": round(100 * attn_tflops / 2250.0, 2),
                 "selection_pct_hbm": round(100 * idx_gbs / peaks["hbm_gbs"], 2),
             },
@@ -682,16 +732,21 @@ def main(argv=None) -> int:
                 "achieved": round(attn_tflops, 1), "peak": peak_t, "unit": "TFLOP/s",
                 "frac": round(attn_tflops / peak_t, 4), "traffic": traffic.get("attention"),
                 "traffic_unit": "bytes per launch (ncu, DRAM read + write)",
-                "peak_source": f"{peak_src} bf16_tflops_sustained",
+                "traffic_source": "recorded constant from an earlier ncu capture of this workload, "
+                                  "not measured in this run",
+                "peak_source": f"{peak_src} bf16_tflops (burst)",
             },
             "roofline_index_stage": {
                 "bound": "hbm", "kernel": "pool_pipe_kernel + select_tc_kernel",
                 "achieved": round(idx_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(idx_gbs / peaks["hbm_gbs"], 4), "traffic": traffic.get("index_stage"),
                 "traffic_unit": "bytes per launch pair (ncu, DRAM read + write)",
+                "traffic_source": "recorded constant from an earlier ncu capture of this workload, "
+                                  "not measured in this run",
                 "algorithmic_bytes": idx_bytes_rank, "peak_source": f"{peak_src} hbm_gbs",
             },
             "cpu_baseline": cpu,
+            "parity": parity,
             "e2e": e2e,
             "gpu_launches": 3 * args.steps,
             "clocks": clocks.summary(),

@@ -263,7 +263,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         good = __shfl_sync(0xffffffffu, good, 0);
         if (!good) return false;
       } else {
-        // Float32 pooled inputs: gather the listed rows, rounding to the compute dtype.
+        // Float32 pooled inputs: gather up to 64 listed entries in two parts --
+        // rows e < 64 hold round(x), rows 64 + e hold round(x - round(x)) -- so
+        // the softmax can add the two score columns and P.V covers both parts.
         if (lane == 0) {
           good = mbar_wait(smem_u32(&k_empty[st]), par, wc);
           if (good) good = mbar_wait(smem_u32(&v_empty[st]), par, wc);
@@ -275,17 +277,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int e = idx / kChunks, cidx = idx % kChunks;
           const int hh = cidx >> 3, cc = cidx & 7;
           const uint32_t off = hh * 16384 + e * 128 + ((cc ^ (e & 7)) << 4);
+          const int ent = e & 63;
+          const bool low = e >= 64;
           uint4 kvk = make_uint4(0, 0, 0, 0), kvv = make_uint4(0, 0, 0, 0);
-          if (e < rec.nvalid && cidx * 8 < a.D) {
-            const int blk = clampi(a.pr_ids[lrow + rec.kstart + e], 0, a.Nb - 1);
+          if (ent < rec.nvalid && cidx * 8 < a.D) {
+            const int blk = clampi(a.pr_ids[lrow + rec.kstart + ent], 0, a.Nb - 1);
             const long long src = ((long long)h * a.Nb + blk) * a.D + cidx * 8;
             const float4* fk = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.pk) + src);
             const float4* fv = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.pv) + src);
             const float4 k0 = __ldg(fk), k1 = __ldg(fk + 1), v0 = __ldg(fv), v1 = __ldg(fv + 1);
-            kvk = make_uint4(pack2<DT>(k0.x, k0.y), pack2<DT>(k0.z, k0.w), pack2<DT>(k1.x, k1.y),
-                             pack2<DT>(k1.z, k1.w));
-            kvv = make_uint4(pack2<DT>(v0.x, v0.y), pack2<DT>(v0.z, v0.w), pack2<DT>(v1.x, v1.y),
-                             pack2<DT>(v1.z, v1.w));
+            kvk = make_uint4(pack2_split<DT>(k0.x, k0.y, low), pack2_split<DT>(k0.z, k0.w, low),
+                             pack2_split<DT>(k1.x, k1.y, low), pack2_split<DT>(k1.z, k1.w, low));
+            kvv = make_uint4(pack2_split<DT>(v0.x, v0.y, low), pack2_split<DT>(v0.z, v0.w, low),
+                             pack2_split<DT>(v1.x, v1.y, low), pack2_split<DT>(v1.z, v1.w, low));
           }
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(kst + off), "r"(kvk.x),
                        "r"(kvk.y), "r"(kvk.z), "r"(kvk.w)
@@ -345,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           n_corr_items += any != 0u;
         }
       } else if (npr > 0) {
-        n_corr_items = (npr + 127) / 128;
+        n_corr_items = (npr + 63) / 64;   // 64 entries (high + low parts) per item
       }
       const int n_items = n_sel_items + n_corr_items;
       // Q tiles of both chunks (a work item without keys needs none).
@@ -412,7 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();   // pmask reads done before the next work item clears it
       } else {
         for (int j = 0; j < n_corr_items && ok; ++j)
-          ok = emit(make_rec(KIND_CORR, j * 128, min(128, npr - j * 128)), pr.h, lrow);
+          ok = emit(make_rec(KIND_CORR, j * 64, min(64, npr - j * 64)), pr.h, lrow);
       }
       if (ok && n_items == 0) ok = emit(make_rec(KIND_EMPTY, 0, 0), pr.h, lrow);
     }
@@ -576,6 +580,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
 #pragma unroll
         for (int c = 0; c < 4; ++c) reg_fence(s[c]);
+        if (rec.kind == KIND_CORR) {
+          // Key rows 64..127 of a gathered tile are the low parts of entries
+          // 0..63: s = S[:, j] + S[:, 64 + j], copied to both halves, so P.V
+          // multiplies the same P by the high and by the low parts.
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              s[c][j] = __float_as_uint(__uint_as_float(s[c][j]) + __uint_as_float(s[c + 2][j]));
+              s[c + 2][j] = s[c][j];
+            }
+        }
         // validity of the 128 entries; a warp with any invalid entry masks on every lane
         float bias = 0.f;
         uint32_t vm[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
@@ -594,12 +610,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           full = false;
 #pragma unroll
           for (int c = 0; c < 4; ++c) vm[c] = rec.mask[c];
-        } else {   // KIND_CORR
+        } else {   // KIND_CORR: entries 0..63, duplicated in columns 64..127
           bias = a.corr_shift;
-          full = rec.nvalid >= 128;
+          full = rec.nvalid >= 64;
           if (!full) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) vm[c] = prefix_mask(rec.nvalid - 32 * c);
+            for (int c = 0; c < 4; ++c) vm[c] = prefix_mask(rec.nvalid - 32 * (c & 1));
           }
         }
         // Full warps keep the raw scores (c2 > 0 keeps the order; x = s*c2 + bias
@@ -687,7 +703,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_u32(&p_full[2 * x + h]));
         }
-        l += ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
+        {
+          // a CORR item's entries appear twice (high and low halves): count them once
+          const float sum = ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
+          l += rec.kind == KIND_CORR ? 0.5f * sum : sum;
+        }
         ++kv;
         ++pv_cnt;
       }

@@ -30,8 +30,12 @@
 // producer streams contiguous 128-row tiles of the head's pooled K/V with TMA
 // and ships a 128-bit mask per tile (bit = "this pooled entry is in the pruned
 // list"); masked entries take finite_min logits, exactly like list padding in
-// the reference kernel. Tiles without a pruned entry are skipped. (Pooled
-// inputs in float32 are rounded on a gathered path instead.)
+// the reference kernel. Tiles without a pruned entry are skipped. Pooled
+// inputs in float32 (the semantics of fpv2/reference.py) take a gathered path
+// that keeps their precision: each CORR item holds up to 64 pruned entries,
+// key/value rows 0..63 the 16-bit high parts and rows 64..127 the low parts
+// (x - high); the softmax adds the two score columns of an entry, and the two
+// PV halves multiply the same P by the high and by the low parts.
 //
 // Warp roles (320 threads, one persistent CTA per SM):
 //   warp 0     producer: takes work items from a global counter (largest
@@ -102,7 +106,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = o_free + 1;          // [1]
   uint64_t* lbar = drain + 1;            // [4] epilogue (m_h, l_h) exchange of a warp pair
   uint64_t* obar = lbar + 4;             // [2] output tile staged (per 64-column box)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(obar + 2);
+  uint64_t* cbar = obar + 2;             // [4] S tile of a CORR item read by both warps of a quarter
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cbar + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -134,6 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&lbar[i]), 2);
     mbar_init(smem_u32(&obar[0]), D == 128 ? 4 : 8);
     mbar_init(smem_u32(&obar[1]), 4);
+    for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&cbar[i]), 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -224,7 +230,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         good = __shfl_sync(0xffffffffu, good, 0);
         if (!good) return false;
       } else {
-        // Float32 pooled inputs: gather the listed rows, rounding to the compute dtype.
+        // Float32 pooled inputs: gather up to 64 listed entries in two parts --
+        // rows e < 64 hold round(x), rows 64 + e hold round(x - round(x)) -- so
+        // that Q.K^T over both parts carries the float32 pooled keys (the
+        // softmax adds the two score columns) and P.V over both parts the
+        // float32 pooled values.
         if (lane == 0) {
           good = mbar_wait(smem_u32(&k_empty[st]), par, wc);
           if (good) good = mbar_wait(smem_u32(&v_empty[st]), par, wc);
@@ -236,17 +246,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int e = idx / kChunks, cidx = idx % kChunks;
           const int hh = cidx >> 3, cc = cidx & 7;
           const uint32_t off = hh * 16384 + e * 128 + ((cc ^ (e & 7)) << 4);
+          const int ent = e & 63;
+          const bool low = e >= 64;
           uint4 kvk = make_uint4(0, 0, 0, 0), kvv = make_uint4(0, 0, 0, 0);
-          if (e < rec.nvalid && cidx * 8 < a.D) {
-            const int blk = clampi(a.pr_ids[lrow + rec.kstart + e], 0, a.Nb - 1);
+          if (ent < rec.nvalid && cidx * 8 < a.D) {
+            const int blk = clampi(a.pr_ids[lrow + rec.kstart + ent], 0, a.Nb - 1);
             const long long src = ((long long)ck.h * a.Nb + blk) * a.D + cidx * 8;
             const float4* fk = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.pk) + src);
             const float4* fv = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.pv) + src);
             const float4 k0 = __ldg(fk), k1 = __ldg(fk + 1), v0 = __ldg(fv), v1 = __ldg(fv + 1);
-            kvk = make_uint4(pack2<DT>(k0.x, k0.y), pack2<DT>(k0.z, k0.w), pack2<DT>(k1.x, k1.y),
-                             pack2<DT>(k1.z, k1.w));
-            kvv = make_uint4(pack2<DT>(v0.x, v0.y), pack2<DT>(v0.z, v0.w), pack2<DT>(v1.x, v1.y),
-                             pack2<DT>(v1.z, v1.w));
+            kvk = make_uint4(pack2_split<DT>(k0.x, k0.y, low), pack2_split<DT>(k0.z, k0.w, low),
+                             pack2_split<DT>(k1.x, k1.y, low), pack2_split<DT>(k1.z, k1.w, low));
+            kvv = make_uint4(pack2_split<DT>(v0.x, v0.y, low), pack2_split<DT>(v0.z, v0.w, low),
+                             pack2_split<DT>(v1.x, v1.y, low), pack2_split<DT>(v1.z, v1.w, low));
           }
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(kst + off), "r"(kvk.x),
                        "r"(kvk.y), "r"(kvk.z), "r"(kvk.w)
@@ -322,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           n_corr_items += any != 0u;
         }
       } else if (npr > 0) {
-        n_corr_items = (npr + 127) / 128;
+        n_corr_items = (npr + 63) / 64;   // 64 entries (high + low parts) per item
       }
       const int n_items = max(1, n_sel_items + n_corr_items);
       int emitted = 0;
@@ -370,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();   // pmask reads done before the next work item clears it
       } else {
         for (int j = 0; j < n_corr_items && ok; ++j)
-          ok = emit(make_rec(KIND_CORR, j * 128, min(128, npr - j * 128)), ck, lrow);
+          ok = emit(make_rec(KIND_CORR, j * 64, min(64, npr - j * 64)), ck, lrow);
       }
       if (ok && n_sel_items + n_corr_items == 0) ok = emit(make_rec(KIND_EMPTY, 0, 0), ck, lrow);
     }
@@ -508,6 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool row_valid = false;
     float m_used = kFiniteMin, l = 0.f;   // this half's running max and sum
     int pv_wi = 0;
+    int ncorr = 0;                        // CORR items seen (cbar phase)
     bool stored = false;                  // this thread issued output tensor stores
     while (ok) {
       const int ri = icount % kRecs;
@@ -544,6 +557,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         reg_fence(s[0]);
         reg_fence(s[1]);
+        if (rec.kind == KIND_CORR) {
+          // Key rows 64..127 of a gathered tile are the low parts of entries
+          // 0..63: both warps of the lane quarter form s = S[:, j] + S[:, 64 + j]
+          // (their own columns plus the other half's; the same sum either way),
+          // then wait for each other before either overwrites its columns with P.
+          const uint32_t other = tmem_base + lane_off + C::kSCol + st * 128 + (half ^ 1) * 64;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t t[32];
+            tmem_ld32(other + 32 * c, t);
+            tmem_wait_ld();
+            reg_fence(t);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              s[c][j] = __float_as_uint(__uint_as_float(s[c][j]) + __uint_as_float(t[j]));
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&cbar[quarter]));
+          ok = mbar_wait(smem_u32(&cbar[quarter]), ncorr & 1, wc);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+          ++ncorr;
+        }
         // validity of this warp's 64 entries; a mixed warp masks on every lane
         float bias = 0.f;
         uint32_t vm0 = 0xffffffffu, vm1 = 0xffffffffu;
@@ -563,9 +601,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           full = false;
           vm0 = rec.mask[2 * half];
           vm1 = rec.mask[2 * half + 1];
-        } else {   // KIND_CORR
+        } else {   // KIND_CORR: both halves hold the same (at most 64) entries
           bias = a.corr_shift;
-          const int nv = rec.nvalid - half * 64;
+          const int nv = rec.nvalid;
           full = nv >= 64;
           if (!full) {
             vm0 = nv >= 32 ? 0xffffffffu : (nv <= 0 ? 0u : ((1u << nv) - 1u));
@@ -654,7 +692,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             pk[16 * c + q] = pack_p<DT>(pv.x, pv.y);
           }
         }
-        l += ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
+        // A CORR item's probabilities count once, in half 0's sum: half 1 only
+        // adds P times the low parts of the pooled values to O_1 (relative to its
+        // own m_1, so the epilogue's weights combine both terms correctly).
+        if (rec.kind != KIND_CORR || half == 0)
+          l += ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
         // P_h -> the first 32 columns of this half's own S columns (already read)
         tmem_st32(s_tmem, pk);
         tmem_wait_st();
@@ -800,7 +842,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int D>
 size_t smem_bytes() {
   return 1024 + (size_t)(2 + 2 * kStages) * Cfg<D>::kTileBytes + sizeof(Rec) * kRecs +
-         4 * kMaskWordsMax + 4 * (4 * 128 + 4 * 128) + 8 * (4 + 2 * kRecs + 7 * kStages + 10) + 16;
+         4 * kMaskWordsMax + 4 * (4 * 128 + 4 * 128) + 8 * (4 + 2 * kRecs + 7 * kStages + 14) + 16;
 }
 
 }  // namespace

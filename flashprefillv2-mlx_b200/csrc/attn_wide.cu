@@ -185,23 +185,27 @@ __global__ void __launch_bounds__(kWThreads, 1)
         }
         if (!good) return false;
       } else {
-        // Float32 pooled inputs: gather the listed rows, rounding to the compute
-        // dtype; K first (its slot frees with the previous QK), then V (its slot
-        // frees with the previous PV, which is issued after this item's QK).
+        // Float32 pooled inputs: gather up to 64 listed entries in two parts --
+        // rows e < 64 hold round(x), rows 64 + e hold round(x - round(x)) -- so
+        // the softmax can add the two score columns and P.V covers both parts;
+        // K first (its slot frees with the previous QK), then V (its slot frees
+        // with the previous PV, which is issued after this item's QK).
         auto gather = [&](const void* src_base, uint32_t dst) {
           constexpr int kChunks = kD / 8;   // 16-byte chunks per row
           for (int idx = lane; idx < 128 * kChunks; idx += 32) {
             const int e = idx / kChunks, cidx = idx % kChunks;
             const int hh = cidx >> 3, cc = cidx & 7;
             const uint32_t off = hh * 16384 + e * 128 + ((cc ^ (e & 7)) << 4);
+            const int ent = e & 63;
+            const bool low = e >= 64;
             uint4 val = make_uint4(0, 0, 0, 0);
-            if (e < rec.nvalid) {
-              const int blk = clampi(a.pr_ids[lrow + rec.kstart + e], 0, a.Nb - 1);
+            if (ent < rec.nvalid) {
+              const int blk = clampi(a.pr_ids[lrow + rec.kstart + ent], 0, a.Nb - 1);
               const long long src = ((long long)ck.h * a.Nb + blk) * kD + cidx * 8;
               const float4* f = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src_base) + src);
               const float4 x0 = __ldg(f), x1 = __ldg(f + 1);
-              val = make_uint4(pack2<DT>(x0.x, x0.y), pack2<DT>(x0.z, x0.w), pack2<DT>(x1.x, x1.y),
-                               pack2<DT>(x1.z, x1.w));
+              val = make_uint4(pack2_split<DT>(x0.x, x0.y, low), pack2_split<DT>(x0.z, x0.w, low),
+                               pack2_split<DT>(x1.x, x1.y, low), pack2_split<DT>(x1.z, x1.w, low));
             }
             asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst + off), "r"(val.x),
                          "r"(val.y), "r"(val.z), "r"(val.w)
@@ -279,7 +283,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
           n_corr_items += any != 0u;
         }
       } else if (npr > 0) {
-        n_corr_items = (npr + 127) / 128;
+        n_corr_items = (npr + 63) / 64;   // 64 entries (high + low parts) per item
       }
       const int n_items = max(1, n_sel_items + n_corr_items);
       int emitted = 0;
@@ -327,7 +331,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
         __syncwarp();   // mask reads done before the next work item clears it
       } else {
         for (int j = 0; j < n_corr_items && ok; ++j)
-          ok = emit(make_rec(KIND_CORR, j * 128, min(128, npr - j * 128)), ck, lrow);
+          ok = emit(make_rec(KIND_CORR, j * 64, min(64, npr - j * 64)), ck, lrow);
       }
       if (ok && n_sel_items + n_corr_items == 0) ok = emit(make_rec(KIND_EMPTY, 0, 0), ck, lrow);
     }
@@ -500,6 +504,18 @@ __global__ void __launch_bounds__(kWThreads, 1)
         reg_fence(s[1]);
         reg_fence(s[2]);
         reg_fence(s[3]);
+        if (rec.kind == KIND_CORR) {
+          // Key rows 64..127 of a gathered tile are the low parts of entries
+          // 0..63: s = S[:, j] + S[:, 64 + j], copied to both halves, so P.V
+          // multiplies the same P by the high and by the low parts.
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              s[c][j] = __float_as_uint(__uint_as_float(s[c][j]) + __uint_as_float(s[c + 2][j]));
+              s[c + 2][j] = s[c][j];
+            }
+        }
         // Validity of the 128 keys; a warp with any invalid entry masks on every lane.
         float bias = 0.f;
         uint32_t vm[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
@@ -521,13 +537,13 @@ __global__ void __launch_bounds__(kWThreads, 1)
           full = false;
 #pragma unroll
           for (int c = 0; c < 4; ++c) vm[c] = rec.mask[c];
-        } else {   // KIND_CORR
+        } else {   // KIND_CORR: entries 0..63, duplicated in columns 64..127
           bias = a.corr_shift;
-          full = rec.nvalid >= 128;
+          full = rec.nvalid >= 64;
           if (!full) {
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
-              const int n = rec.nvalid - 32 * c;
+              const int n = rec.nvalid - 32 * (c & 1);
               vm[c] = n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
             }
           }
@@ -615,7 +631,11 @@ __global__ void __launch_bounds__(kWThreads, 1)
             else pk1[16 * (c - 2) + q] = pack_p<DT>(pv.x, pv.y);
           }
         }
-        l += ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
+        {
+          // a CORR item's entries appear twice (high and low halves): count them once
+          const float sum = ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
+          l += rec.kind == KIND_CORR ? 0.5f * sum : sum;
+        }
         // P of keys [0, 128) -> S columns [0, 64) (already read)
         tmem_st32(s_tmem, pk0);
         tmem_st32(s_tmem + 32, pk1);

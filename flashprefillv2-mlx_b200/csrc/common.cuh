@@ -74,6 +74,17 @@ template <> __device__ __forceinline__ float2 unpack2<DT_F16>(uint32_t v) {
   return __half22float2(h);
 }
 
+// Two-term split of float32 values into 16-bit pairs: the high part is
+// round(x), the low part round(x - round(x)). Their sum carries about 16 (bf16)
+// or 22 (fp16) significant bits, so a product accumulated over both parts in
+// fp32 matches the float32 product to within float32 rounding.
+template <int DT> __device__ __forceinline__ uint32_t pack2_split(float lo, float hi, bool low_part) {
+  const uint32_t h = pack2<DT>(lo, hi);
+  if (!low_part) return h;
+  const float2 r = unpack2<DT>(h);
+  return pack2<DT>(lo - r.x, hi - r.y);
+}
+
 // Packing of softmax probabilities p in [0, 2^16] for the P.V MMA. For bf16 the
 // conversion is done on the integer units (round half up on the 16 dropped
 // bits, then a byte permute), which keeps it off the pipe that evaluates ex2;

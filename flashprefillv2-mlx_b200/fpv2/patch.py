@@ -191,6 +191,13 @@ def _causal_offset(q: torch.Tensor, k: torch.Tensor, attn_mask: object, is_causa
     return None
 
 
+def _needs_autograd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> bool:
+    """True when the call must record a backward graph (grad mode on and an input
+    that requires grad). The FPV2 kernels have no backward, so such a call goes
+    to torch's own SDPA, which records one; inference and ``no_grad`` calls do not."""
+    return torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad)
+
+
 def _eligible(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -276,7 +283,7 @@ def enable(
         if call_config is not None:
             call_config = _request_config(call_config, key.shape[-2], total_tokens)
         offset = _causal_offset(query, key, attn_mask, is_causal)
-        if call_config is not None and _eligible(
+        if call_config is not None and not _needs_autograd(query, key, value) and _eligible(
             query, key, value, offset, dropout_p, enable_gqa, kwargs, call_config, min_tokens
         ):
             call_scale = query.shape[-1] ** -0.5 if scale is None else scale

@@ -185,15 +185,22 @@ def block_scores_and_select(
     query_length: int | None = None,
     precision: str = "fp32",
     keep_scores: bool | None = None,
+    only_tiles=None,
 ) -> SelectionResult:
     """Selection mask ``[Hkv, Nt, Nb]`` following fpv2/selection.py:109-201.
 
     ``precision`` is "fp32" (the reference's arithmetic) or "fp64" (used to
     classify threshold flips).  Raw scores are kept only when the query-tile
-    chunking is off, as in selection.py:196-201.
+    chunking is off, as in selection.py:196-201.  ``only_tiles`` (not in the
+    reference) evaluates only the listed query tiles, each on its own; every
+    tile's selection depends on its own rows alone, so the result rows equal
+    the corresponding rows of the full mask, shaped ``[Hkv, len(only_tiles), Nb]``.
+    ``q`` may be any float array; it is converted to float32 per tile chunk.
     """
     config = as_config(config)
-    q = np.asarray(q, dtype=np.float32)
+    q = np.asarray(q)
+    if q.dtype not in (np.float32, np.float16, np.float64):
+        q = q.astype(np.float32)
     pooled_k = np.asarray(pooled_k, dtype=np.float32)
     valid_length = q.shape[-2] if query_length is None else query_length
     query_heads, kv_heads, padded_length, num_blocks = _validate_select(
@@ -202,12 +209,17 @@ def block_scores_and_select(
     ftype = np.float64 if precision == "fp64" else np.float32
     group = query_heads // kv_heads
     num_tiles = padded_length // config.tile_q
-    grouped_q = q.reshape(kv_heads, group, padded_length, q.shape[-1]).astype(ftype)
+    grouped_q = q.reshape(kv_heads, group, padded_length, q.shape[-1])
     pk = pooled_k.astype(ftype)
     block_starts = np.arange(num_blocks, dtype=np.int64) * config.block_k
     block_ends = block_starts + config.block_k
     sink = block_starts < config.sink_tokens
     chunk_tiles = config.score_chunk_tiles or num_tiles
+    if only_tiles is None:
+        groups = [(t, min(t + chunk_tiles, num_tiles)) for t in range(0, num_tiles, chunk_tiles)]
+    else:
+        groups = [(int(t), int(t) + 1) for t in only_tiles]
+        keep_scores = False
     if keep_scores is None:
         keep_scores = config.score_chunk_tiles is None
     selected_chunks, energy_chunks, thr_chunks = [], [], []
@@ -218,15 +230,15 @@ def block_scores_and_select(
     )
     scale_f = ftype(scale)
     alpha_f = ftype(np.float32(config.alpha))
-    for tile_start in range(0, num_tiles, chunk_tiles):
-        tile_end = min(tile_start + chunk_tiles, num_tiles)
+    for tile_start, tile_end in groups:
         row_start = tile_start * config.tile_q
         row_end = tile_end * config.tile_q
         row_ids = np.arange(row_start, row_end, dtype=np.int64)
         tile_ids = np.arange(tile_start, tile_end, dtype=np.int64)
         tile_first = offset + tile_ids * config.tile_q
         tile_last = np.minimum(tile_first + config.tile_q, offset + valid_length) - 1
-        scores = np.matmul(grouped_q[:, :, row_start:row_end, :], pk.transpose(0, 2, 1)[:, None])
+        rows_q = grouped_q[:, :, row_start:row_end, :].astype(np.float32).astype(ftype)
+        scores = np.matmul(rows_q, pk.transpose(0, 2, 1)[:, None])
         scores = scores * scale_f
         if raw_scores is not None:
             raw_scores[:, :, row_start:row_end, :] = scores
@@ -353,6 +365,7 @@ def sparse_attention(
     *, scale: float, config: Any = None, offset: int = 0,
     query_length: int | None = None, key_length: int | None = None,
     dtype: str = "bf16", tiles: list[tuple[int, int]] | None = None,
+    pooled_dtype: str | None = None, p_dtype: str | None = None, out_dtype: str | None = None,
 ) -> np.ndarray:
     """List-driven FPV2 attention, fpv2/kernel.py:187-414 and 441-590.
 
@@ -363,9 +376,15 @@ def sparse_attention(
     to ``dtype`` as the kernel stores it (kernel.py:409).  Rows at or beyond
     ``query_length`` are padding and are returned as zeros.  ``tiles``
     restricts the evaluation to the listed (kv_head, tile) pairs.
+
+    Rounding controls (not in the reference; they decompose the error budget
+    of an implementation): ``pooled_dtype`` overrides the cast of the pooled
+    K/V ("fp32" keeps them), ``p_dtype`` rounds the probabilities P to a
+    16-bit type before the P.V product (the row sums keep the unrounded P),
+    ``out_dtype`` overrides the rounding of the stored output ("fp32": none).
     """
     config = as_config(config)
-    q = np.asarray(q, np.float32)
+    q = np.asarray(q)
     k = np.asarray(k, np.float32)
     v = np.asarray(v, np.float32)
     hq, lq_pad, d = q.shape
@@ -375,8 +394,8 @@ def sparse_attention(
     nb = lk_pad // config.block_k
     valid_q = lq_pad if query_length is None else query_length
     valid_k = lk_pad if key_length is None else key_length
-    pk = round_to(np.asarray(pooled_k, np.float32), dtype)
-    pv = round_to(np.asarray(pooled_v, np.float32), dtype)
+    pk = round_to(np.asarray(pooled_k, np.float32), pooled_dtype or dtype)
+    pv = round_to(np.asarray(pooled_v, np.float32), pooled_dtype or dtype)
     sel_ids = np.clip(selected_ids, 0, nb - 1)
     sel_counts = np.clip(selected_counts, 0, nb)
     pr_ids = np.clip(pruned_ids, 0, nb - 1)
@@ -392,7 +411,7 @@ def sparse_attention(
         if rows.size == 0:
             continue
         positions = offset + rows
-        qt = q[h * g:(h + 1) * g][:, rows, :]                     # [g, r, d]
+        qt = q[h * g:(h + 1) * g][:, rows, :].astype(np.float32)   # [g, r, d]
         key_idx = []
         for b in sel_ids[h, t, : sel_counts[h, t]]:
             start = int(b) * config.block_k
@@ -411,9 +430,10 @@ def sparse_attention(
             vals = np.concatenate([vals, pv[h, blocks]], axis=0)
         m = s.max(axis=-1, keepdims=True) if s.shape[-1] else np.zeros((g, rows.size, 1), np.float32)
         p = np.exp2(s - m)
-        o = np.matmul(p, vals) / p.sum(axis=-1, keepdims=True)
+        pr = p if p_dtype is None else round_to(p.astype(np.float32), p_dtype)
+        o = np.matmul(pr, vals) / p.sum(axis=-1, keepdims=True)
         out[h * g:(h + 1) * g, rows, :] = o
-    return round_to(out, dtype)
+    return round_to(out, out_dtype or dtype)
 
 
 def exact_causal_attention(q, k, v, scale: float, offset: int = 0) -> np.ndarray:
@@ -502,7 +522,7 @@ def fpv2_attention_blockwise(
     evaluated (the others stay zero).
     """
     config = as_config(config)
-    q = np.asarray(q, np.float32)
+    q = np.asarray(q)
     k = np.asarray(k, np.float32)
     v = np.asarray(v, np.float32)
     hq, lq, d = q.shape
@@ -524,7 +544,7 @@ def fpv2_attention_blockwise(
     for h, t in tiles:
         rows = np.arange(t * config.tile_q, (t + 1) * config.tile_q)
         positions = offset + rows
-        qt = q[h * g:(h + 1) * g][:, rows, :]
+        qt = q[h * g:(h + 1) * g][:, rows, :].astype(np.float32)
         blocks = np.nonzero(selected[h, t])[0]
         keys = (blocks[:, None] * config.block_k + np.arange(config.block_k)[None, :]).reshape(-1)
         s = np.matmul(qt, k[h, keys].T) * sc
@@ -581,8 +601,11 @@ def causal_block_count(kv_heads: int, query_length: int, offset: int, config: An
     return count * kv_heads
 
 
-def fpv2_sdpa(q, k, v, *, scale: float, config: Any = None, dtype: str = "bf16"):
-    """fpv2/patch.py:102-174 on ``[1, H, L, D]`` float32 arrays of ``dtype`` values."""
+def fpv2_sdpa(q, k, v, *, scale: float, config: Any = None, dtype: str = "bf16",
+              out_dtype: str | None = None):
+    """fpv2/patch.py:102-174 on ``[1, H, L, D]`` float32 arrays of ``dtype`` values.
+
+    ``out_dtype`` ("fp32": unrounded) overrides the rounding of the output."""
     config = as_config(config)
     q = np.asarray(q, np.float32)
     k = np.asarray(k, np.float32)
@@ -615,6 +638,6 @@ def fpv2_sdpa(q, k, v, *, scale: float, config: Any = None, dtype: str = "bf16")
     lists = compact_block_indices(sel, config=config, offset=offset, query_length=lq, key_length=lk)
     out = sparse_attention(
         pq, pk, pv, pooled_k, pooled_v, *lists, scale=scale, config=config,
-        offset=offset, query_length=lq, key_length=lk, dtype=dtype,
+        offset=offset, query_length=lq, key_length=lk, dtype=dtype, out_dtype=out_dtype,
     )
     return out[None, :, :lq, :], sel, lists

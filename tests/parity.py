@@ -102,3 +102,66 @@ def attention_errors(actual: torch.Tensor, expected: np.ndarray, rows: int | Non
         expected = expected[:, :rows]
     err = np.abs(a - expected)
     return float(err.max()), float(err.mean())
+
+
+# ---------------------------------------------------------------------------
+# sampled checks of full-size layers (64k / 128k): a fixed set of query tiles
+# ---------------------------------------------------------------------------
+
+
+def sample_tiles(num_tiles: int, *, extra: int = 4, seed: int = 0) -> list[int]:
+    """First, quartile, middle and last tiles (the last two are the dense tail)
+    plus ``extra`` seeded random tiles."""
+    base = {0, 1, num_tiles // 4, num_tiles // 2, (3 * num_tiles) // 4,
+            num_tiles - 3, num_tiles - 2, num_tiles - 1}
+    rng = np.random.default_rng(seed)
+    base |= {int(x) for x in rng.integers(0, num_tiles, size=extra)}
+    return sorted(t for t in base if 0 <= t < num_tiles)
+
+
+def tile_positions(tiles, tile_q: int, valid_length: int) -> np.ndarray:
+    pos = np.concatenate([np.arange(t * tile_q, (t + 1) * tile_q) for t in tiles])
+    return pos[pos < valid_length]
+
+
+def check_selection_tiles(q_np: np.ndarray, pooled_k_np: np.ndarray, gpu_rows: np.ndarray, tiles,
+                          *, scale: float, config, offset: int = 0,
+                          query_length: int | None = None) -> SelectCheck:
+    """GPU mask rows ``[Hkv, len(tiles), Nb]`` vs the oracle evaluated on those tiles
+    only, flips allowed only in the fp64 band."""
+    c = O.as_config(config)
+    kw = dict(scale=scale, config=c, offset=offset, query_length=query_length, only_tiles=tiles)
+    r32 = O.block_scores_and_select(q_np, pooled_k_np, **kw)
+    r64 = O.block_scores_and_select(q_np, pooled_k_np, precision="fp64", **kw)
+    band = O.threshold_band(r64, FLIP_REL_BAND)
+    diff = gpu_rows != r32.selected
+    return SelectCheck(
+        mismatches=int(diff.sum()),
+        flips_in_band=int((diff & band).sum()),
+        out_of_band=int((diff & ~band).sum()),
+        band_blocks=int(band.sum()),
+    )
+
+
+def check_lists_tiles(gpu_rows: np.ndarray, list_rows, tiles, *, config, offset: int,
+                      query_length: int, key_length: int) -> bool:
+    """Each sampled tile's full-width GPU lists equal the oracle's compaction of the
+    GPU mask row (a one-tile compaction whose offset is the tile's first position)."""
+    c = O.as_config(config)
+    for i, t in enumerate(tiles):
+        first = t * c.tile_q
+        ql = min(c.tile_q, query_length - first)
+        if ql <= 0:
+            continue
+        ref = O.compact_block_indices(gpu_rows[:, i:i + 1], config=c, offset=offset + first,
+                                      query_length=ql, key_length=key_length)
+        for got, exp in zip(list_rows, ref):
+            if not np.array_equal(got[:, i:i + 1], exp):
+                return False
+    return True
+
+
+def rows_of(x: torch.Tensor, positions: np.ndarray) -> np.ndarray:
+    """Query rows ``positions`` of a ``[H, L, D]`` tensor as float32 NumPy."""
+    idx = torch.as_tensor(positions, device=x.device)
+    return x.index_select(1, idx).to("cpu", torch.float32).numpy()

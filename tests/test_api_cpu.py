@@ -181,6 +181,33 @@ def test_causal_bias_fall_through_is_bit_identical_on_cpu():
     assert torch.equal(actual, expected)
 
 
+def test_calls_that_need_autograd_are_not_claimed():
+    """The kernels have no backward: with grad mode on and an input that requires
+    grad the hook leaves the call to torch (which records the graph); inference
+    and no_grad calls stay claimable."""
+    import torch.nn.functional as F
+
+    from fpv2.patch import _ORIGINAL_SDPA, _needs_autograd
+
+    q = torch.randn(1, 4, 8, 16, requires_grad=True)
+    k = torch.randn(1, 4, 8, 16)
+    assert _needs_autograd(q, k, k)
+    assert not _needs_autograd(q.detach(), k, k)
+    with torch.no_grad():
+        assert not _needs_autograd(q, k, k)
+    with torch.inference_mode():
+        assert not _needs_autograd(torch.randn(1, 4, 8, 16), k, k)
+    fpv2.enable(min_tokens=1)
+    try:
+        out = F.scaled_dot_product_attention(q, k, k, is_causal=True)
+    finally:
+        fpv2.disable()
+    assert out.grad_fn is not None
+    assert torch.equal(out, _ORIGINAL_SDPA(q, k, k, is_causal=True))
+    out.sum().backward()
+    assert q.grad is not None
+
+
 def test_sdpa_from_host_validates_before_touching_the_gpu():
     import fpv2
 

@@ -20,7 +20,7 @@ from fpv2 import _lib
 from fpv2.patch import _ORIGINAL_SDPA, _effective_config, _request_config
 from oracle import fpv2_oracle as O
 from tests import parity as P
-from tests.synthetic import structured_qkv, uniform_qkv
+from tests.synthetic import structured_qkv, topic_qkv, uniform_qkv
 
 pytestmark = pytest.mark.gpu
 KATS = json.loads((Path(__file__).parent / "golden" / "reference_kats.json").read_text())
@@ -170,6 +170,56 @@ def test_tile_aligned_chunks_match_single_shot_fpv2():
                                      scale=scale, config=chunk_config))
     actual = torch.cat(chunks, dim=2)
     assert rel_err(actual, expected) < 1e-2
+
+
+def test_eligible_shape_that_needs_autograd_falls_through():
+    """An otherwise eligible call whose inputs require grad goes to torch's SDPA
+    (bit-identical, with a backward graph); the same call under no_grad is FPV2."""
+    q, k, v = inputs(4096)
+    q.requires_grad_(True)
+    scale = 64 ** -0.5
+    expected = stock(q, k, v, scale)
+    fpv2.enable(fpv2.FPV2Config(alpha=1.0), min_tokens=1)   # sparse: only forced blocks and the max
+    actual = hooked(q, k, v, scale)
+    assert actual.grad_fn is not None and torch.equal(actual, expected)
+    actual.float().sum().backward()
+    assert q.grad is not None
+    with torch.no_grad():
+        sparse = hooked(q, k, v, scale)
+    assert sparse.grad_fn is None and not torch.equal(sparse, expected)
+
+
+def test_chunked_prefill_with_total_tokens_matches_oracle():
+    """A 16k prompt of the topic-block generator (config 2 shape) prefilled in
+    2048-token chunks through the hook, ``total_tokens`` known: the first chunk is
+    below ``min_tokens`` and goes to the stock path, the others are FPV2 with
+    ``offset = end - 2048`` and the dense tail only at the last chunk
+    (fpv2/patch.py:55-63, 197-198). Every chunk is compared with the oracle's
+    restatement of that call at float32 output, and block sparsity is well above 0."""
+    L, chunk, min_tokens = 16384, 2048, 4096
+    q, k, v = topic_qkv(length=L, query_heads=32, kv_heads=8, head_dim=128, seed=5,
+                        dtype=torch.bfloat16)
+    q4, k4, v4 = q[None].to(DEV), k[None].to(DEV), v[None].to(DEV)
+    cfg = fpv2.FPV2Config(alpha=0.1)
+    scale = 128 ** -0.5
+    fpv2.enable(cfg, min_tokens=min_tokens, collect_stats=True, total_tokens=L)
+    outs = [hooked(q4[:, :, end - chunk:end], k4[:, :, :end], v4[:, :, :end], scale)
+            for end in range(chunk, L + 1, chunk)]
+    sparsity = fpv2.block_sparsity()
+    fpv2.disable()
+    assert _lib.device_status() == 0
+    assert sparsity > 0.3, sparsity
+    qf, kf, vf = P.np32(q), P.np32(k), P.np32(v)
+    for i, end in enumerate(range(chunk, L + 1, chunk)):
+        qc = qf[:, end - chunk:end]
+        if end < min_tokens:
+            exp = O.exact_causal_attention(qc, kf[:, :end], vf[:, :end], scale, offset=end - chunk)
+        else:
+            c = O.request_config(cfg, end, L)
+            exp = O.fpv2_sdpa(qc[None], kf[None, :, :end], vf[None, :, :end], scale=scale, config=c,
+                              dtype="bf16", out_dtype="fp32")[0][0]
+        mx, mean = P.attention_errors(outs[i][0], exp)
+        assert mx <= P.MAX_ABS_TOL and mean <= P.MEAN_ABS_TOL, (end, mx, mean)
 
 
 def test_block_sparsity_includes_dense_gated_prefill():

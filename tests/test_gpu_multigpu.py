@@ -83,9 +83,13 @@ def test_head_parallel_two_gpus_matches_single_gpu(length, hq, hkv, d):
     for p in procs:
         p.start()
     results = dict(queue.get(timeout=300) for _ in procs)
+    # No rank is ever killed here (a rank's output buffer may be bound to an
+    # NVLink multicast object): one that outlives the join fails the test and
+    # leaves on its own through the kernels' bounded waits and the process
+    # group's 60 s timeout.
     for p in procs:
         p.join(timeout=120)
-        if p.is_alive():  # pragma: no cover
-            p.kill()
+    alive = [p.pid for p in procs if p.is_alive()]
+    assert not alive, f"ranks still running after 120 s (pids {alive})"
     for rank in (0, 1):
         assert results[rank].startswith("maxdiff 0.0 0.0 0.0 multicast"), results[rank]

@@ -311,6 +311,31 @@ def test_attention_parity(case):
     assert mx_r <= P.MAX_ABS_TOL and mean_r <= P.MEAN_ABS_TOL, (mx_r, mean_r)
 
 
+GQA8_CASES = [
+    # Hq, Hkv, length, dtype, corr: G = 8 packs 16 query positions x 8 heads per
+    # 128-row tile (fpv2/patch.py:41-52), the packing of config 5
+    (16, 2, 4096, torch.bfloat16, True),
+    (16, 2, 4096, torch.float16, False),
+    (64, 8, 4096, torch.float16, True),
+    (64, 8, 4096, torch.bfloat16, False),
+    (64, 8, 8192, torch.bfloat16, True),
+]
+
+
+@pytest.mark.parametrize("case", GQA8_CASES, ids=lambda c: f"Hq{c[0]}-Hkv{c[1]}-L{c[2]}-{c[3]}-corr{c[4]}")
+def test_attention_parity_gqa8(case):
+    hq, hkv, length, dtype, corr = case
+    q, k, v = topic_qkv(length=length, query_heads=hq, kv_heads=hkv, head_dim=128, seed=hq + length,
+                        dtype=dtype)
+    cfg = _effective_config(fpv2.FPV2Config(alpha=0.1, mean_correction=corr), hq, hkv)
+    assert cfg.tile_q == 16
+    out, kern, out_ref, ref = _attention_case(q, k, v, cfg)
+    mx_k, mean_k = P.kernel_errors(out, kern)
+    assert mx_k <= P.KERNEL_MAX_ABS_TOL and mean_k <= P.KERNEL_MEAN_ABS_TOL, (mx_k, mean_k)
+    mx_r, mean_r = P.attention_errors(out_ref, ref)
+    assert mx_r <= P.MAX_ABS_TOL and mean_r <= P.MEAN_ABS_TOL, (mx_r, mean_r)
+
+
 @pytest.mark.parametrize("offset,query_length", [(1024, 1024), (1920, 128)])
 def test_attention_chunk_offsets(offset, query_length):
     """Reference tests/test_kernel.py:135-160 (chunk offsets)."""
