@@ -508,7 +508,8 @@ def main(argv=None) -> int:
         if mc is not None:
             from fpv2.shard import head_parallel_sdpa
 
-            return head_parallel_sdpa(qd, kd, vd, scale=scale, config=base_cfg, fused=True)
+            return head_parallel_sdpa(qd, kd, vd, scale=scale, config=base_cfg, fused=True,
+                                      copy=False)
         out = fpv2.fpv2_sdpa(qd, kd, vd, scale=scale, config=base_cfg)
         if world > 1:
             import torch.distributed as dist

@@ -27,9 +27,30 @@ struct Rec {
   int kind;
   int kstart;     // SEL: first key; POOL: first pooled row; CORR: first list entry
   int nvalid;     // CORR: valid list entries in this chunk
-  int flags;      // bit 0: first item of the work item, bit 1: last item
+  int flags;      // bit 0: first item of the work unit, bit 1: last item
   int w;          // work item index
+  int part;       // -1: the unit is a whole work item; else its partial-result slot
   uint32_t mask[4];   // POOL: entry e is a pruned block when bit (e & 31) of mask[e >> 5]
+};
+
+// KV-segment split of long work items (attn_tc_kernel). A work item w <
+// max_slots whose KV item count exceeds 2 * seg_len is cut into nseg <= kMaxSeg
+// contiguous segments of its KV item sequence: the CTA that takes the item
+// queues segments 1.. for the other CTAs and runs segment 0; every segment
+// writes its unnormalised output with its row maxima and sums, and
+// attn_combine_kernel merges them. Slots are the item indices themselves, so
+// which items split does not depend on timing.
+constexpr int kMaxSeg = 16;
+constexpr int kSegLen = 64;     // target KV items per segment
+
+struct Split {
+  int* hdr;            // [0] work counter, [1] queue tail, [2] queue head
+  int* flags;          // [qcap] queue entry written (zeroed before launch)
+  int4* entries;       // [qcap] (w, segment, nseg, 0)
+  int4* recs;          // [max_slots] (w, nseg, 0, 0); nseg 0 = not split (zeroed before launch)
+  float* partials;     // [max_slots][kMaxSeg][128 * Dt + 256]: O rows, then m[128], l[128]
+  int max_slots;       // 0: no split
+  int qcap;
 };
 
 
@@ -38,9 +59,11 @@ struct Params {
   int nch;          // 128-row chunks per tile
   int items;        // total work items
   uint32_t idesc_qk, idesc_pv;
+  uint32_t idesc_qk64;  // Q.K^T with N = 64 (the two key parts of a gathered CORR item)
   int* sched;       // work counter (zeroed before launch); null = static round robin
   int* status;
   long long budget;
+  Split split;      // attn_tc_kernel only
 };
 
 struct Chunk {

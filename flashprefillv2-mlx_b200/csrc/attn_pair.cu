@@ -108,7 +108,8 @@ __device__ __forceinline__ uint32_t prefix_mask(long long n) {
   return n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
 }
 
-template <int D, int DT>
+// DT: input dtype; VT: operand type of the P.V product (V and P).
+template <int D, int DT, int VT>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
                      const __grid_constant__ CUtensorMap tmap_k,
@@ -231,10 +232,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           const CUtensorMap* mk = rec.kind == KIND_SEL ? &tmap_k : &tmap_pk;
           const CUtensorMap* mv = rec.kind == KIND_SEL ? &tmap_v : &tmap_pv;
-          const bool paged = rec.kind == KIND_SEL && a.block_table != nullptr;
+          // (a converted V copy is contiguous even when the page pools are not)
+          const bool paged_k = rec.kind == KIND_SEL && a.block_table != nullptr;
+          const bool paged_v = paged_k && a.v_conv == nullptr;
           // One 128-row tile: a 3-D box per 64 features, or, from a page pool,
           // one 4-D box per page the 128 keys span.
-          auto load_tile = [&](uint32_t dst, const CUtensorMap* m, uint32_t bar) {
+          auto load_tile = [&](uint32_t dst, const CUtensorMap* m, uint32_t bar, bool paged) {
             mbar_arrive_expect_tx(bar, (uint32_t)C::kTileBytes);
             if (!paged) {
 #pragma unroll
@@ -255,17 +258,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           };
           good = mbar_wait(smem_u32(&k_empty[st]), par, wc);
           if (good) {
-            load_tile(kst, mk, smem_u32(&k_full[st]));
+            load_tile(kst, mk, smem_u32(&k_full[st]), paged_k);
             good = mbar_wait(smem_u32(&v_empty[st]), par, wc);
           }
-          if (good) load_tile(vst, mv, smem_u32(&v_full[st]));
+          if (good) load_tile(vst, mv, smem_u32(&v_full[st]), paged_v);
         }
         good = __shfl_sync(0xffffffffu, good, 0);
         if (!good) return false;
       } else {
         // Float32 pooled inputs: gather up to 64 listed entries in two parts --
         // rows e < 64 hold round(x), rows 64 + e hold round(x - round(x)) -- so
-        // the softmax can add the two score columns and P.V covers both parts.
+        // that Q.K^T accumulated over both parts carries the float32 pooled keys
+        // and P.V over both parts the float32 pooled values.
         if (lane == 0) {
           good = mbar_wait(smem_u32(&k_empty[st]), par, wc);
           if (good) good = mbar_wait(smem_u32(&v_empty[st]), par, wc);
@@ -288,8 +292,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float4 k0 = __ldg(fk), k1 = __ldg(fk + 1), v0 = __ldg(fv), v1 = __ldg(fv + 1);
             kvk = make_uint4(pack2_split<DT>(k0.x, k0.y, low), pack2_split<DT>(k0.z, k0.w, low),
                              pack2_split<DT>(k1.x, k1.y, low), pack2_split<DT>(k1.z, k1.w, low));
-            kvv = make_uint4(pack2_split<DT>(v0.x, v0.y, low), pack2_split<DT>(v0.z, v0.w, low),
-                             pack2_split<DT>(v1.x, v1.y, low), pack2_split<DT>(v1.z, v1.w, low));
+            const float vs = a.v_exp != nullptr ? ldexpf(1.f, -a.v_exp[h]) : 1.f;
+            kvv = make_uint4(pack2_split<VT>(v0.x * vs, v0.y * vs, low),
+                             pack2_split<VT>(v0.z * vs, v0.w * vs, low),
+                             pack2_split<VT>(v1.x * vs, v1.y * vs, low),
+                             pack2_split<VT>(v1.z * vs, v1.w * vs, low));
           }
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(kst + off), "r"(kvk.x),
                        "r"(kvk.y), "r"(kvk.z), "r"(kvk.w)
@@ -379,6 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         r.nvalid = nvalid;
         r.flags = (emitted == 0 ? 1 : 0) | (emitted == max(1, n_items) - 1 ? 2 : 0);
         r.w = w;
+        r.part = -1;
         r.mask[0] = r.mask[1] = r.mask[2] = r.mask[3] = 0u;
         ++emitted;
         return r;
@@ -424,6 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       Rec done;
       done.kind = KIND_DONE;
       done.kstart = done.nvalid = done.w = 0;
+      done.part = -1;
       done.flags = 3;
       done.mask[0] = done.mask[1] = done.mask[2] = done.mask[3] = 0u;
       emit(done, 0, 0);
@@ -449,23 +458,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       int qs[2] = {0, 0};
       bool ok = true;
       int pb = -1;                 // kv index whose PV_B is pending
-      bool pb_first = false, pb_last = false;
-      auto issue_qk = [&](int x, int st) {
+      bool pb_first = false, pb_last = false, pb_corr = false;
+      auto issue_qk = [&](int x, int st, bool corr) {
         const uint32_t s_tmem = tmem_base + C::kSCol + x * 128;
         const uint32_t qb = q_smem + qs[x] * C::kTileBytes;
         const uint32_t kb = k_smem + st * C::kTileBytes;
+        if (!corr) {
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const int hh = kk / 4, sub = kk % 4;
-          const uint64_t adesc = sw128_desc(qb + hh * 16384 + sub * 32, 16, 1024);
-          const uint64_t bdesc = sw128_desc(kb + hh * 16384 + sub * 32, 16, 1024);
-          umma_ss(s_tmem, adesc, bdesc, p.idesc_qk, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int hh = kk / 4, sub = kk % 4;
+            const uint64_t adesc = sw128_desc(qb + hh * 16384 + sub * 32, 16, 1024);
+            const uint64_t bdesc = sw128_desc(kb + hh * 16384 + sub * 32, 16, 1024);
+            umma_ss(s_tmem, adesc, bdesc, p.idesc_qk, kk > 0 ? 1u : 0u);
+          }
+        } else {
+          // gathered CORR item: S[:, 0:64] = Q.K_high^T + Q.K_low^T (key rows 0..63
+          // and 64..127, 8 KB apart in each 64-column box), N = 64, one accumulator
+#pragma unroll
+          for (int part = 0; part < 2; ++part) {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const int hh = kk / 4, sub = kk % 4;
+              const uint64_t adesc = sw128_desc(qb + hh * 16384 + sub * 32, 16, 1024);
+              const uint64_t bdesc = sw128_desc(kb + hh * 16384 + part * 8192 + sub * 32, 16, 1024);
+              umma_ss(s_tmem, adesc, bdesc, p.idesc_qk64, (part | kk) ? 1u : 0u);
+            }
+          }
         }
         umma_commit(smem_u32(&s_full[x]));
       };
       // O_x += P_x V, each 64-key half as soon as its four softmax warps are done;
       // P (128 keys, 16-bit pairs) sits in the first 64 of the S columns.
-      auto issue_pv = [&](int x, int n, bool first, bool last) -> bool {
+      auto issue_pv = [&](int x, int n, bool first, bool last, bool corr) -> bool {
         const int st = n % kStages;
         const uint32_t par = (n / kStages) & 1;
         if (!mbar_wait(smem_u32(&v_full[st]), par, wc)) return false;
@@ -475,10 +499,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int h = 0; h < 2; ++h) {
           if (!mbar_wait(smem_u32(&p_full[2 * x + h]), n & 1, wc)) return false;
           tc_fence_after();
+          // (CORR: P of the 64 entries times the high value rows 0..63, then the
+          // same P times the low value rows 64..127)
+          const uint32_t pcol = corr ? 0u : 32u * h;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t bdesc = sw128_desc(vst + (4 * h + kk) * 2048, 16384, 1024);
-            umma_ts(tmem_base + C::kOCol + x * 128, s_tmem + 32 * h + kk * 8, bdesc, p.idesc_pv,
+            umma_ts(tmem_base + C::kOCol + x * 128, s_tmem + pcol + kk * 8, bdesc, p.idesc_pv,
                     (first && h == 0 && kk == 0) ? 0u : 1u);
           }
         }
@@ -510,24 +537,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           qcount += 2;
         }
         tc_fence_after();
-        issue_qk(0, st);
+        const bool corr = rec.kind == KIND_CORR;
+        issue_qk(0, st, corr);
         if (last) umma_commit(smem_u32(&q_empty[qs[0]]));
         if (pb >= 0) {
-          ok = issue_pv(1, pb, pb_first, pb_last);
+          ok = issue_pv(1, pb, pb_first, pb_last, pb_corr);
           if (!ok) break;
           pb = -1;
         }
-        issue_qk(1, st);
+        issue_qk(1, st, corr);
         umma_commit(smem_u32(&k_empty[st]));
         if (last) umma_commit(smem_u32(&q_empty[qs[1]]));
-        ok = issue_pv(0, kv, first, last);
+        ok = issue_pv(0, kv, first, last, corr);
         if (!ok) break;
         pb = kv;
         pb_first = first;
         pb_last = last;
+        pb_corr = corr;
         ++kv;
       }
-      if (ok && pb >= 0) issue_pv(1, pb, pb_first, pb_last);
+      if (ok && pb >= 0) issue_pv(1, pb, pb_first, pb_last, pb_corr);
       umma_commit(smem_u32(drain));
       mbar_wait(smem_u32(drain), 0, wc, false);
     }
@@ -545,6 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int icount = 0, kv = 0, nfull = 0;
     bool ok = true;
     long long row = 0, position = 0, head = 0;
+    int kvh = 0;
     bool row_valid = false;
     float m_used = kFiniteMin, l = 0.f;
     int pv_cnt = 0;
@@ -560,6 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (rec.kind == KIND_DONE) break;
       if (rec.flags & 1) {
         const Pair pr = make_pair(p, rec.w);
+        kvh = pr.h;
         const int P = pr.c[x] * 128 + r;
         row = (long long)pr.t * a.tile_q + P % a.tile_q;
         head = (long long)pr.h * a.G + P / a.tile_q;
@@ -580,18 +611,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
 #pragma unroll
         for (int c = 0; c < 4; ++c) reg_fence(s[c]);
-        if (rec.kind == KIND_CORR) {
-          // Key rows 64..127 of a gathered tile are the low parts of entries
-          // 0..63: s = S[:, j] + S[:, 64 + j], copied to both halves, so P.V
-          // multiplies the same P by the high and by the low parts.
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              s[c][j] = __float_as_uint(__uint_as_float(s[c][j]) + __uint_as_float(s[c + 2][j]));
-              s[c + 2][j] = s[c][j];
-            }
-        }
         // validity of the 128 entries; a warp with any invalid entry masks on every lane
         float bias = 0.f;
         uint32_t vm[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
@@ -610,12 +629,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           full = false;
 #pragma unroll
           for (int c = 0; c < 4; ++c) vm[c] = rec.mask[c];
-        } else {   // KIND_CORR: entries 0..63, duplicated in columns 64..127
+        } else {   // KIND_CORR (at most 64 entries)
           bias = a.corr_shift;
-          full = rec.nvalid >= 64;
+          full = rec.nvalid >= 128;
           if (!full) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) vm[c] = prefix_mask(rec.nvalid - 32 * (c & 1));
+            for (int c = 0; c < 4; ++c) vm[c] = prefix_mask(rec.nvalid - 32 * c);
           }
         }
         // Full warps keep the raw scores (c2 > 0 keeps the order; x = s*c2 + bias
@@ -646,7 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mt = full ? fmaf(m4, c2, bias) : m4;
         }
         const float m_new = fmaxf(m_used, mt);
-        const bool need = m_new > m_used + RescaleT<DT>::value ||
+        const bool need = m_new > m_used + RescaleT<VT>::value ||
                           (m_used == kFiniteMin && m_new > kFiniteMin);
         if (__any_sync(0xffffffffu, need)) {
           const float f = need ? ex2(m_used - m_new) : 1.f;
@@ -693,7 +712,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               pv.x = ex2(xv.x);
               pv.y = ex2(xv.y);
               rs[q & 3] = add_f32x2(rs[q & 3], pv);
-              pk[16 * cc + q] = pack_p<DT>(pv.x, pv.y);
+              pk[16 * cc + q] = pack_p<VT>(pv.x, pv.y);
             }
           }
           // P of keys 64h .. 64h+63 -> S columns 32h .. 32h+31 (already read)
@@ -703,17 +722,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_u32(&p_full[2 * x + h]));
         }
-        {
-          // a CORR item's entries appear twice (high and low halves): count them once
-          const float sum = ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
-          l += rec.kind == KIND_CORR ? 0.5f * sum : sum;
-        }
+        l += ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
         ++kv;
         ++pv_cnt;
       }
       if (rec.flags & 2) {
         // ---- output row: O / l, written straight from registers
-        const float inv = (pv_cnt > 0 && l > 0.f) ? 1.f / l : 0.f;
+        // (times 2^v_exp[h] when V was scaled into the fp16 range)
+        const float vsc = a.v_exp != nullptr ? ldexpf(1.f, a.v_exp[kvh]) : 1.f;
+        const float inv = (pv_cnt > 0 && l > 0.f) ? vsc / l : 0.f;
         if (pv_cnt > 0) {
           ok = mbar_wait(smem_u32(&o_full[x]), nfull & 1, wc);
           ok = __all_sync(0xffffffffu, ok);
@@ -778,8 +795,10 @@ cudaError_t launch_attn_pair(const AttnArgs& a, const TcLaunch& L, int* sched, c
   p.nch = (a.G * a.tile_q) / 128;
   p.items = a.Hkv * a.Nt * (p.nch / 2);
   const int fmt = a.dt == DT_BF16 ? 1 : 0;
+  const int vdt = a.vdt < 0 ? a.dt : a.vdt;
   p.idesc_qk = umma_idesc_f16(fmt, 128, 128, 0, 0);
-  p.idesc_pv = umma_idesc_f16(fmt, 128, a.D, 0, 1);
+  p.idesc_qk64 = umma_idesc_f16(fmt, 128, 64, 0, 0);
+  p.idesc_pv = umma_idesc_f16(vdt == DT_BF16 ? 1 : 0, 128, a.D, 0, 1);
   p.sched = sched;
   p.status = L.status;
   p.budget = L.budget;
@@ -792,20 +811,22 @@ cudaError_t launch_attn_pair(const AttnArgs& a, const TcLaunch& L, int* sched, c
     e = cudaMemsetAsync(sched, 0, sizeof(int), stream);
     if (e != cudaSuccess) return e;
   }
-#define FPV2_PAIR_LAUNCH(DD, TT)                                                            \
+#define FPV2_PAIR_LAUNCH(DD, TT, VV)                                                        \
   {                                                                                         \
     const size_t smem = pair_smem_bytes<DD>();                                              \
-    e = cudaFuncSetAttribute(attn_pair_kernel<DD, TT>,                                      \
+    e = cudaFuncSetAttribute(attn_pair_kernel<DD, TT, VV>,                                  \
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
     if (e != cudaSuccess) return e;                                                         \
-    attn_pair_kernel<DD, TT><<<grid, kThreads, smem, stream>>>(m[0], m[1], m[2], m[3], m[4], p); \
+    attn_pair_kernel<DD, TT, VV><<<grid, kThreads, smem, stream>>>(m[0], m[1], m[2], m[3], m[4], p); \
   }
-  if (a.D == 64 && a.dt == DT_BF16) FPV2_PAIR_LAUNCH(64, DT_BF16)
-  else if (a.D == 64 && a.dt == DT_F16) FPV2_PAIR_LAUNCH(64, DT_F16)
+  if (a.D == 64 && a.dt == DT_BF16 && vdt == DT_F16) FPV2_PAIR_LAUNCH(64, DT_BF16, DT_F16)
+  else if (a.D == 64 && a.dt == DT_BF16) FPV2_PAIR_LAUNCH(64, DT_BF16, DT_BF16)
+  else if (a.D == 64 && a.dt == DT_F16) FPV2_PAIR_LAUNCH(64, DT_F16, DT_F16)
   // head_dim 96 runs on the 128-wide tiles (TMA zero-fills columns 96..127,
   // PV runs with N = 96, output rows stop at column 96)
-  else if (a.D >= 96 && a.dt == DT_BF16) FPV2_PAIR_LAUNCH(128, DT_BF16)
-  else if (a.D >= 96 && a.dt == DT_F16) FPV2_PAIR_LAUNCH(128, DT_F16)
+  else if (a.D >= 96 && a.dt == DT_BF16 && vdt == DT_F16) FPV2_PAIR_LAUNCH(128, DT_BF16, DT_F16)
+  else if (a.D >= 96 && a.dt == DT_BF16) FPV2_PAIR_LAUNCH(128, DT_BF16, DT_BF16)
+  else if (a.D >= 96 && a.dt == DT_F16) FPV2_PAIR_LAUNCH(128, DT_F16, DT_F16)
   else return cudaErrorInvalidValue;
 #undef FPV2_PAIR_LAUNCH
   return cudaGetLastError();

@@ -34,8 +34,9 @@
 // inputs in float32 (the semantics of fpv2/reference.py) take a gathered path
 // that keeps their precision: each CORR item holds up to 64 pruned entries,
 // key/value rows 0..63 the 16-bit high parts and rows 64..127 the low parts
-// (x - high); the softmax adds the two score columns of an entry, and the two
-// PV halves multiply the same P by the high and by the low parts.
+// (x - high). The issuer accumulates Q.K_high^T + Q.K_low^T into the same 64
+// score columns (two N = 64 chains) and P.V_high + P.V_low into O_0, so the
+// softmax sees an ordinary 64-entry item (its second half fully masked).
 //
 // Warp roles (320 threads, one persistent CTA per SM):
 //   warp 0     producer: takes work items from a global counter (largest
@@ -66,7 +67,10 @@ struct Cfg {
   static constexpr int kSCol = 256;                // S buffers at 256, 384
 };
 
-template <int D, int DT>
+// DT: input dtype; VT: operand type of the P.V product (V and P); GATHER: the
+// pooled correction is gathered from float32 pooled K/V (CORR items) instead of
+// streamed as pooled tiles (compiled out of the other instantiations).
+template <int D, int DT, int VT, bool GATHER>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                    const __grid_constant__ CUtensorMap tmap_k,
@@ -106,8 +110,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = o_free + 1;          // [1]
   uint64_t* lbar = drain + 1;            // [4] epilogue (m_h, l_h) exchange of a warp pair
   uint64_t* obar = lbar + 4;             // [2] output tile staged (per 64-column box)
-  uint64_t* cbar = obar + 2;             // [4] S tile of a CORR item read by both warps of a quarter
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cbar + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(obar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -139,7 +142,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&lbar[i]), 2);
     mbar_init(smem_u32(&obar[0]), D == 128 ? 4 : 8);
     mbar_init(smem_u32(&obar[1]), 4);
-    for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&cbar[i]), 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -160,12 +162,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   WaitCtx wc{p.status, abort_flag, p.budget};
   const int bk_sub = a.block_k / 128;
-  const bool pool_tiles = a.corr && a.pooled_dt == DT;   // TMA pooled tiles vs gather
+  const bool pool_tiles = a.corr && !GATHER;   // TMA pooled tiles vs gather
 
   if (warp == 0) {
     // ============================ producer ================================
     int qcount = 0, icount = 0, kv = 0, wstatic = blockIdx.x;
     bool ok = true;
+    const bool split = p.split.max_slots > 0 && p.sched != nullptr;
     auto next_work = [&]() -> int {
       int w = 0;
       if (p.sched != nullptr) {
@@ -176,6 +179,62 @@ __global__ void __launch_bounds__(kThreads, 1)
         wstatic += gridDim.x;
       }
       return w;
+    };
+    // Next work unit: a queued segment of a split item first, else the next
+    // work item (seg 0, nseg 0 = not decided yet). False when no work is left.
+    auto next_unit = [&](int& w, int& seg, int& nseg) -> bool {
+      if (split) {
+        int got = -1;
+        if (lane == 0) {
+          // lock-free pop: every failed CAS means another CTA took an entry
+          while (true) {
+            const int tail = atomicAdd(&p.split.hdr[1], 0);
+            const int head = atomicAdd(&p.split.hdr[2], 0);
+            if (head >= tail) break;
+            if (atomicCAS(&p.split.hdr[2], head, head + 1) == head) {
+              got = head;
+              break;
+            }
+          }
+        }
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (got >= 0) {
+          int4 e = make_int4(0, 0, 0, 0);
+          bool good = true;
+          if (lane == 0) {
+            // the pusher reserved the entry before writing it: bounded wait for its flag
+            const volatile int* f = p.split.flags + got;
+            const long long t0 = clock64();
+            while (*f == 0) {
+              if (*wc.abort_flag) { good = false; break; }
+              if (clock64() - t0 > wc.budget) {
+                atomicOr(wc.status, STATUS_TIMEOUT);
+                *wc.abort_flag = 1;
+                good = false;
+                break;
+              }
+            }
+            if (good) {
+              __threadfence();
+              const volatile int* ev = reinterpret_cast<const volatile int*>(p.split.entries + got);
+              e = make_int4(ev[0], ev[1], ev[2], ev[3]);
+            }
+          }
+          good = __shfl_sync(0xffffffffu, good, 0);
+          if (!good) {
+            ok = false;
+            return false;
+          }
+          w = __shfl_sync(0xffffffffu, e.x, 0);
+          seg = __shfl_sync(0xffffffffu, e.y, 0);
+          nseg = __shfl_sync(0xffffffffu, e.z, 0);
+          return true;
+        }
+      }
+      w = next_work();
+      seg = 0;
+      nseg = 0;
+      return w < p.items;
     };
     // Publish one record; SEL/POOL/CORR records are followed by their K/V tiles.
     auto emit = [&](const Rec& rec, const Chunk& ck, long long lrow) -> bool {
@@ -198,10 +257,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           const CUtensorMap* mk = rec.kind == KIND_SEL ? &tmap_k : &tmap_pk;
           const CUtensorMap* mv = rec.kind == KIND_SEL ? &tmap_v : &tmap_pv;
-          const bool paged = rec.kind == KIND_SEL && a.block_table != nullptr;
+          // (a converted V copy is contiguous even when the page pools are not)
+          const bool paged_k = rec.kind == KIND_SEL && a.block_table != nullptr;
+          const bool paged_v = paged_k && a.v_conv == nullptr;
           // One 128-row tile: a single 3-D box per 64 features, or, from a page
           // pool, one 4-D box per page the 128 keys span.
-          auto load_tile = [&](uint32_t dst, const CUtensorMap* m, uint32_t bar) {
+          auto load_tile = [&](uint32_t dst, const CUtensorMap* m, uint32_t bar, bool paged) {
             mbar_arrive_expect_tx(bar, (uint32_t)C::kTileBytes);
             if (!paged) {
 #pragma unroll
@@ -222,19 +283,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           };
           good = mbar_wait(smem_u32(&k_empty[st]), par, wc);
           if (good) {
-            load_tile(kst, mk, smem_u32(&k_full[st]));
+            load_tile(kst, mk, smem_u32(&k_full[st]), paged_k);
             good = mbar_wait(smem_u32(&v_empty[st]), par, wc);
           }
-          if (good) load_tile(vst, mv, smem_u32(&v_full[st]));
+          if (good) load_tile(vst, mv, smem_u32(&v_full[st]), paged_v);
         }
         good = __shfl_sync(0xffffffffu, good, 0);
         if (!good) return false;
       } else {
         // Float32 pooled inputs: gather up to 64 listed entries in two parts --
         // rows e < 64 hold round(x), rows 64 + e hold round(x - round(x)) -- so
-        // that Q.K^T over both parts carries the float32 pooled keys (the
-        // softmax adds the two score columns) and P.V over both parts the
-        // float32 pooled values.
+        // that Q.K^T accumulated over both parts carries the float32 pooled keys
+        // and P.V over both parts the float32 pooled values.
         if (lane == 0) {
           good = mbar_wait(smem_u32(&k_empty[st]), par, wc);
           if (good) good = mbar_wait(smem_u32(&v_empty[st]), par, wc);
@@ -257,8 +317,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float4 k0 = __ldg(fk), k1 = __ldg(fk + 1), v0 = __ldg(fv), v1 = __ldg(fv + 1);
             kvk = make_uint4(pack2_split<DT>(k0.x, k0.y, low), pack2_split<DT>(k0.z, k0.w, low),
                              pack2_split<DT>(k1.x, k1.y, low), pack2_split<DT>(k1.z, k1.w, low));
-            kvv = make_uint4(pack2_split<DT>(v0.x, v0.y, low), pack2_split<DT>(v0.z, v0.w, low),
-                             pack2_split<DT>(v1.x, v1.y, low), pack2_split<DT>(v1.z, v1.w, low));
+            const float vs = a.v_exp != nullptr ? ldexpf(1.f, -a.v_exp[ck.h]) : 1.f;
+            kvv = make_uint4(pack2_split<VT>(v0.x * vs, v0.y * vs, low),
+                             pack2_split<VT>(v0.z * vs, v0.w * vs, low),
+                             pack2_split<VT>(v1.x * vs, v1.y * vs, low),
+                             pack2_split<VT>(v1.z * vs, v1.w * vs, low));
           }
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(kst + off), "r"(kvk.x),
                        "r"(kvk.y), "r"(kvk.z), "r"(kvk.w)
@@ -278,7 +341,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
 
-    for (int w = next_work(); w < p.items && ok; w = next_work()) {
+    int w = 0, seg = 0, nseg = 0;
+    while (ok && next_unit(w, seg, nseg)) {
       const Chunk ck = make_chunk(p, w);
       const long long lrow = ((long long)ck.h * a.Nt + ck.t) * a.Nb;
       const int nsel = clampi(a.sel_counts[(long long)ck.h * a.Nt + ck.t], 0, a.Nb);
@@ -336,8 +400,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else if (npr > 0) {
         n_corr_items = (npr + 63) / 64;   // 64 entries (high + low parts) per item
       }
-      const int n_items = max(1, n_sel_items + n_corr_items);
-      int emitted = 0;
+      const int n_total = n_sel_items + n_corr_items;
+      // First visit of a long item with a slot: cut it into segments and queue
+      // segments 1.. for the other CTAs (this CTA runs segment 0).
+      if (split && nseg == 0 && w < p.split.max_slots && n_total > 2 * kSegLen) {
+        const int want = min(kMaxSeg, (n_total + kSegLen - 1) / kSegLen);
+        if (lane == 0) {
+          p.split.recs[w] = make_int4(w, want, 0, 0);
+          const int base = atomicAdd(&p.split.hdr[1], want - 1);
+          for (int s2 = 1; s2 < want; ++s2)
+            p.split.entries[base + s2 - 1] = make_int4(w, s2, want, 0);
+          __threadfence();
+          for (int s2 = 1; s2 < want; ++s2) atomicExch(&p.split.flags[base + s2 - 1], 1);
+        }
+        nseg = want;
+      }
+      // This unit's share [lo, hi) of the item's KV item sequence.
+      int lo = 0, hi = n_total, part = -1;
+      if (nseg > 0) {
+        const int per = (n_total + nseg - 1) / nseg;
+        lo = min(n_total, seg * per);
+        hi = seg == nseg - 1 ? n_total : min(n_total, lo + per);
+        part = w * kMaxSeg + seg;
+      }
+      const int n_items = max(1, hi - lo);
+      int emitted = 0, kvi = 0;   // kvi: index in the item's KV item sequence
       auto make_rec = [&](int kind, int kstart, int nvalid) {
         Rec r;
         r.kind = kind;
@@ -345,27 +432,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         r.nvalid = nvalid;
         r.flags = (emitted == 0 ? 1 : 0) | (emitted == n_items - 1 ? 2 : 0);
         r.w = w;
+        r.part = part;
         r.mask[0] = r.mask[1] = r.mask[2] = r.mask[3] = 0u;
         ++emitted;
         return r;
       };
-      for (int i0 = 0; i0 < brk && ok; i0 += 32) {
+      for (int i0 = 0; i0 < brk && ok && kvi < hi; i0 += 32) {
         const int i = i0 + lane;
         const int blk = i < brk ? clampi(a.sel_ids[lrow + i], 0, a.Nb - 1) : 0;
         const int cnt = min(32, brk - i0);
-        for (int j = 0; j < cnt && ok; ++j) {
+        for (int j = 0; j < cnt && ok && kvi < hi; ++j) {
           const int bj = __shfl_sync(0xffffffffu, blk, j);
           const long long bstart = (long long)bj * a.block_k;
-          for (int sub = 0; sub < bk_sub && ok; ++sub) {
+          for (int sub = 0; sub < bk_sub && ok && kvi < hi; ++sub) {
             const long long ks = bstart + sub * 128;
             if (ks > ck.abs_last) break;
+            if (kvi++ < lo) continue;
             ok = emit(make_rec(KIND_SEL, (int)ks, 0), ck, lrow);
           }
         }
       }
       if (pool_tiles) {
         const int nwords = (a.Nb + 31) / 32;
-        for (int j = 0; j < n_ptiles && ok && npr > 0; ++j) {
+        for (int j = 0; j < n_ptiles && ok && npr > 0 && kvi < hi; ++j) {
           uint32_t m4[4];
           uint32_t any = 0;
 #pragma unroll
@@ -374,6 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             any |= m4[x];
           }
           if (!any) continue;
+          if (kvi++ < lo) continue;
           Rec r = make_rec(KIND_POOL, j * 128, 0);
 #pragma unroll
           for (int x = 0; x < 4; ++x) r.mask[x] = m4[x];
@@ -381,15 +471,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();   // pmask reads done before the next work item clears it
       } else {
-        for (int j = 0; j < n_corr_items && ok; ++j)
+        for (int j = 0; j < n_corr_items && ok && kvi < hi; ++j) {
+          if (kvi++ < lo) continue;
           ok = emit(make_rec(KIND_CORR, j * 64, min(64, npr - j * 64)), ck, lrow);
+        }
       }
-      if (ok && n_sel_items + n_corr_items == 0) ok = emit(make_rec(KIND_EMPTY, 0, 0), ck, lrow);
+      if (ok && emitted == 0) ok = emit(make_rec(KIND_EMPTY, 0, 0), ck, lrow);
     }
     if (ok) {
       Rec done;
       done.kind = KIND_DONE;
       done.kstart = done.nvalid = done.w = 0;
+      done.part = -1;
       done.flags = 3;
       done.mask[0] = done.mask[1] = done.mask[2] = done.mask[3] = 0u;
       Chunk none{};
@@ -415,7 +508,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int qcount = 0, icount = 0, kv = 0, wi = 0, qs = 0;
       bool ok = true, need_ofree = false, first_pv = true;
       int prev = -1;   // kv index whose PV is pending
-      auto issue_pv = [&](int n) -> bool {
+      bool prev_corr = false;   // that item is a gathered CORR item (high + low parts)
+      auto issue_pv = [&](int n, bool corr) -> bool {
         const int st = n % kStages;
         const uint32_t par = (n / kStages) & 1;
         if (!mbar_wait(smem_u32(&v_full[st]), par, wc)) return false;
@@ -436,6 +530,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t bdesc = sw128_desc(vst + (4 * h + kk) * 2048, 16384, 1024);
             umma_ts(tmem_base + C::kOCol + h * 128, s_tmem + 64 * h + kk * 8, bdesc, p.idesc_pv,
                     (first_pv && kk == 0) ? 0u : 1u);
+          }
+          if (corr && h == 0) {
+            // CORR: the same P_0 times the low parts of the pooled values (rows 64..127)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t bdesc = sw128_desc(vst + (4 + kk) * 2048, 16384, 1024);
+              umma_ts(tmem_base + C::kOCol, s_tmem + kk * 8, bdesc, p.idesc_pv, 1u);
+            }
           }
         }
         first_pv = false;
@@ -471,22 +573,39 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t s_tmem = tmem_base + C::kSCol + st * 128;
           const uint32_t qb = q_smem + qs * C::kTileBytes;
           const uint32_t kb = k_smem + st * C::kTileBytes;
+          const bool corr = GATHER && rec.kind == KIND_CORR;
+          if (!corr) {
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const int hh = kk / 4, sub = kk % 4;
-            const uint64_t adesc = sw128_desc(qb + hh * 16384 + sub * 32, 16, 1024);
-            const uint64_t bdesc = sw128_desc(kb + hh * 16384 + sub * 32, 16, 1024);
-            umma_ss(s_tmem, adesc, bdesc, p.idesc_qk, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const int hh = kk / 4, sub = kk % 4;
+              const uint64_t adesc = sw128_desc(qb + hh * 16384 + sub * 32, 16, 1024);
+              const uint64_t bdesc = sw128_desc(kb + hh * 16384 + sub * 32, 16, 1024);
+              umma_ss(s_tmem, adesc, bdesc, p.idesc_qk, kk > 0 ? 1u : 0u);
+            }
+          } else {
+            // S[:, 0:64] = Q.K_high^T + Q.K_low^T: key rows 0..63 and 64..127 of the
+            // gathered tile (8 KB apart in each 64-column box), N = 64, one accumulator
+#pragma unroll
+            for (int part = 0; part < 2; ++part) {
+#pragma unroll
+              for (int kk = 0; kk < D / 16; ++kk) {
+                const int hh = kk / 4, sub = kk % 4;
+                const uint64_t adesc = sw128_desc(qb + hh * 16384 + sub * 32, 16, 1024);
+                const uint64_t bdesc = sw128_desc(kb + hh * 16384 + part * 8192 + sub * 32, 16, 1024);
+                umma_ss(s_tmem, adesc, bdesc, p.idesc_qk64, (part | kk) ? 1u : 0u);
+              }
+            }
           }
           umma_commit(smem_u32(&s_full[st]));
           umma_commit(smem_u32(&k_empty[st]));
-          if (prev >= 0) ok = issue_pv(prev);
+          if (prev >= 0) ok = issue_pv(prev, prev_corr);
           if (!ok) break;
           prev = kv;
+          prev_corr = corr;
           ++kv;
         }
         if (rec.flags & 2) {   // last item: finish the work item
-          if (prev >= 0) ok = issue_pv(prev);
+          if (prev >= 0) ok = issue_pv(prev, prev_corr);
           if (!ok) break;
           prev = -1;
           umma_commit(smem_u32(&q_empty[qs]));
@@ -520,7 +639,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool row_valid = false;
     float m_used = kFiniteMin, l = 0.f;   // this half's running max and sum
     int pv_wi = 0;
-    int ncorr = 0;                        // CORR items seen (cbar phase)
     bool stored = false;                  // this thread issued output tensor stores
     while (ok) {
       const int ri = icount % kRecs;
@@ -557,31 +675,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         reg_fence(s[0]);
         reg_fence(s[1]);
-        if (rec.kind == KIND_CORR) {
-          // Key rows 64..127 of a gathered tile are the low parts of entries
-          // 0..63: both warps of the lane quarter form s = S[:, j] + S[:, 64 + j]
-          // (their own columns plus the other half's; the same sum either way),
-          // then wait for each other before either overwrites its columns with P.
-          const uint32_t other = tmem_base + lane_off + C::kSCol + st * 128 + (half ^ 1) * 64;
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t t[32];
-            tmem_ld32(other + 32 * c, t);
-            tmem_wait_ld();
-            reg_fence(t);
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              s[c][j] = __float_as_uint(__uint_as_float(s[c][j]) + __uint_as_float(t[j]));
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&cbar[quarter]));
-          ok = mbar_wait(smem_u32(&cbar[quarter]), ncorr & 1, wc);
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) break;
-          tc_fence_after();
-          ++ncorr;
-        }
         // validity of this warp's 64 entries; a mixed warp masks on every lane
         float bias = 0.f;
         uint32_t vm0 = 0xffffffffu, vm1 = 0xffffffffu;
@@ -601,9 +694,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           full = false;
           vm0 = rec.mask[2 * half];
           vm1 = rec.mask[2 * half + 1];
-        } else {   // KIND_CORR: both halves hold the same (at most 64) entries
+        } else {   // KIND_CORR (at most 64 entries: half 1 is all masked)
           bias = a.corr_shift;
-          const int nv = rec.nvalid;
+          const int nv = rec.nvalid - half * 64;
           full = nv >= 64;
           if (!full) {
             vm0 = nv >= 32 ? 0xffffffffu : (nv <= 0 ? 0u : ((1u << nv) - 1u));
@@ -643,7 +736,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mt = full ? fmaf(m4, c2, bias) : m4;
         }
         const float m_new = fmaxf(m_used, mt);
-        const bool need = m_new > m_used + RescaleT<DT>::value ||
+        const bool need = m_new > m_used + RescaleT<VT>::value ||
                           (m_used == kFiniteMin && m_new > kFiniteMin);
         if (__any_sync(0xffffffffu, need)) {
           const float f = need ? ex2(m_used - m_new) : 1.f;
@@ -689,14 +782,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             pv.x = ex2(xv.x);
             pv.y = ex2(xv.y);
             rs[q & 3] = add_f32x2(rs[q & 3], pv);
-            pk[16 * c + q] = pack_p<DT>(pv.x, pv.y);
+            pk[16 * c + q] = pack_p<VT>(pv.x, pv.y);
           }
         }
-        // A CORR item's probabilities count once, in half 0's sum: half 1 only
-        // adds P times the low parts of the pooled values to O_1 (relative to its
-        // own m_1, so the epilogue's weights combine both terms correctly).
-        if (rec.kind != KIND_CORR || half == 0)
-          l += ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
+        l += ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
         // P_h -> the first 32 columns of this half's own S columns (already read)
         tmem_st32(s_tmem, pk);
         tmem_wait_st();
@@ -720,7 +809,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float m_row = fmaxf(m_used, m_o);
         const float a_me = ex2(m_used - m_row), a_o = ex2(m_o - m_row);
         const float lrow = l * a_me + l_o * a_o;
-        const float inv = (pv_wi > 0 && lrow > 0.f) ? 1.f / lrow : 0.f;
+        // (times 2^v_exp[h] when V was scaled into the fp16 range)
+        const float vsc = a.v_exp != nullptr ? ldexpf(1.f, a.v_exp[ck.h]) : 1.f;
+        const float inv = (pv_wi > 0 && lrow > 0.f) ? vsc / lrow : 0.f;
         const float w_lo = (half == 0 ? a_me : a_o) * inv;   // weight of O_0
         const float w_hi = (half == 0 ? a_o : a_me) * inv;   // weight of O_1
         ok = mbar_wait(smem_u32(o_full), wi & 1, wc);
@@ -731,9 +822,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         // completed) in the TMA box layout -- rows of 64 columns, 128-byte
         // swizzle -- and written with one coalesced tensor store per 64-column
         // half; the buffer is released to the producer once the store has read it.
+        // A segment of a split work item (rec.part >= 0) instead writes its
+        // unnormalised output relative to the row maximum m_row, with m_row and
+        // the row sum, to its partial slot for attn_combine_kernel.
         const int qs = wi & 1;
         const uint32_t stage = q_smem + qs * C::kTileBytes;
         const uint32_t o0 = tmem_base + lane_off + C::kOCol + half * (D / 2);
+        float* part = rec.part >= 0 ? p.split.partials + (size_t)rec.part * (128 * D + 256) : nullptr;
 #pragma unroll 1
         for (int dc = 0; dc < D / 64; ++dc) {
           uint32_t x0[32], x1[32];
@@ -746,6 +841,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j) x0[j] = x1[j] = 0u;
+          }
+          if (part != nullptr) {
+            const float a0 = (half == 0 ? a_me : a_o) * vsc, a1 = (half == 0 ? a_o : a_me) * vsc;
+            float4* dst = reinterpret_cast<float4*>(part + r * D + half * (D / 2) + dc * 32);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              dst[j] = make_float4(__uint_as_float(x0[4 * j]) * a0 + __uint_as_float(x1[4 * j]) * a1,
+                                   __uint_as_float(x0[4 * j + 1]) * a0 + __uint_as_float(x1[4 * j + 1]) * a1,
+                                   __uint_as_float(x0[4 * j + 2]) * a0 + __uint_as_float(x1[4 * j + 2]) * a1,
+                                   __uint_as_float(x0[4 * j + 3]) * a0 + __uint_as_float(x1[4 * j + 3]) * a1);
+            continue;
           }
           uint32_t packed[16];
 #pragma unroll
@@ -766,6 +872,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                          : "memory");
           }
         }
+        if (part != nullptr && half == 0) {
+          part[128 * D + r] = m_row;
+          part[128 * D + 128 + r] = lrow;
+        }
         fence_proxy_async_smem();
         // D = 128: each half owns one 64-column box (its 4 warps arrive);
         // D = 64: both halves share the box (all 8 warps arrive, half 0 stores).
@@ -773,7 +883,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&obar[ob]));
         bool good = true;
-        if (a.out_mc != nullptr) {
+        if (part != nullptr) {
+          // nothing staged: release the Q buffer with the store path's arrivals
+          if (a.out_mc != nullptr) {
+            if (lane == 0) mbar_arrive(smem_u32(&q_empty[qs]));
+          } else if (quarter == 0 && lane == 0) {
+            mbar_arrive(smem_u32(&q_empty[qs]));
+          }
+        } else if (a.out_mc != nullptr) {
           // Multicast output: every thread of the box's warps copies 16-byte
           // chunks of the staged box (consecutive threads along a row) to the
           // same place of every rank's full output through the NVLink switch.
@@ -839,10 +956,66 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
 }
 
+// Merge the segments of every split work item: per row,
+//   out = sum_s 2^(m_s - m) O_s / sum_s 2^(m_s - m) l_s,  m = max_s m_s,
+// the same combination the epilogue applies to the two key halves. One CTA per
+// slot (grid-stride), one thread per 8 output columns (one 16-byte store) of a row.
+template <int D, int DT>
+__global__ void __launch_bounds__(512) attn_combine_kernel(Params p) {
+  const AttnArgs& a = p.a;
+  constexpr int kPart = 128 * D + 256;
+  constexpr int kGroups = D / 8;
+  for (int slot = blockIdx.x; slot < p.split.max_slots; slot += gridDim.x) {
+    const int4 rec = p.split.recs[slot];
+    const int nseg = min(rec.y, kMaxSeg);
+    if (nseg <= 0) continue;
+    const Chunk ck = make_chunk(p, rec.x);
+    const float* base = p.split.partials + (size_t)slot * kMaxSeg * kPart;
+    for (int idx = threadIdx.x; idx < 128 * kGroups; idx += blockDim.x) {
+      const int r = idx / kGroups, c0 = (idx % kGroups) * 8;
+      float m = kFiniteMin;
+      for (int sg = 0; sg < nseg; ++sg) m = fmaxf(m, base[(size_t)sg * kPart + 128 * D + r]);
+      float den = 0.f, acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      for (int sg = 0; sg < nseg; ++sg) {
+        const float* ps = base + (size_t)sg * kPart;
+        const float wgt = ex2(ps[128 * D + r] - m);
+        den = fmaf(wgt, ps[128 * D + 128 + r], den);
+        const float4 u0 = *reinterpret_cast<const float4*>(ps + r * D + c0);
+        const float4 u1 = *reinterpret_cast<const float4*>(ps + r * D + c0 + 4);
+        acc[0] = fmaf(wgt, u0.x, acc[0]);
+        acc[1] = fmaf(wgt, u0.y, acc[1]);
+        acc[2] = fmaf(wgt, u0.z, acc[2]);
+        acc[3] = fmaf(wgt, u0.w, acc[3]);
+        acc[4] = fmaf(wgt, u1.x, acc[4]);
+        acc[5] = fmaf(wgt, u1.y, acc[5]);
+        acc[6] = fmaf(wgt, u1.z, acc[6]);
+        acc[7] = fmaf(wgt, u1.w, acc[7]);
+      }
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      const uint4 v = make_uint4(pack2<DT>(acc[0] * inv, acc[1] * inv), pack2<DT>(acc[2] * inv, acc[3] * inv),
+                                 pack2<DT>(acc[4] * inv, acc[5] * inv), pack2<DT>(acc[6] * inv, acc[7] * inv));
+      const int P = ck.c * 128 + r;
+      const long long head = (long long)ck.h * a.G + P / a.tile_q;
+      const long long pos = (long long)ck.t * a.tile_q + P % a.tile_q;
+      if (c0 >= a.D) continue;   // head_dim 96 runs on the 128-wide tiles
+      if (a.out_mc != nullptr) {
+        multimem_st16(reinterpret_cast<char*>(a.out_mc) +
+                          (((head + a.mc_head_offset) * a.Lq_pad + pos) * a.D + c0) * 2, v);
+      } else {
+        *reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.out) +
+                                  ((head * a.Lq_pad + pos) * a.D + c0) * 2) = v;
+      }
+    }
+  }
+  if (a.out_mc != nullptr) asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
 template <int D>
 size_t smem_bytes() {
   return 1024 + (size_t)(2 + 2 * kStages) * Cfg<D>::kTileBytes + sizeof(Rec) * kRecs +
-         4 * kMaskWordsMax + 4 * (4 * 128 + 4 * 128) + 8 * (4 + 2 * kRecs + 7 * kStages + 14) + 16;
+         4 * kMaskWordsMax + 4 * (4 * 128 + 4 * 128) + 8 * (4 + 2 * kRecs + 7 * kStages + 10) + 16;
 }
 
 }  // namespace
@@ -883,60 +1056,164 @@ bool encode_attn_maps(const AttnArgs& a, CUtensorMap (&m)[6]) {
       return false;
   } else {
     if (!encode_tmap_3d(&m[1], a.k, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return false;
-    if (!encode_tmap_3d(&m[2], a.v, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return false;
+    if (a.v_conv == nullptr &&
+        !encode_tmap_3d(&m[2], a.v, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1))
+      return false;
   }
+  const int vdt = a.vdt < 0 ? a.dt : a.vdt;
+  if (a.v_conv != nullptr &&   // converted V copy: contiguous [Hkv, Lk_pad, D]
+      !encode_tmap_3d(&m[2], a.v_conv, vdt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1))
+    return false;
   // Pooled tiles (only read when pooled K/V share the compute dtype).
   const bool pooled_ok = a.corr && a.pooled_dt == a.dt;
   // (pooled tiles unused: q stands in for the pooled tensors)
   if (!encode_tmap_3d(&m[3], pooled_ok ? a.pk : a.q, a.dt, a.D, pooled_ok ? a.Nb : a.Lq_pad,
                       pooled_ok ? a.Hkv : a.Hq, 64, 128, 1))
     return false;
-  if (!encode_tmap_3d(&m[4], pooled_ok ? a.pv : a.q, a.dt, a.D, pooled_ok ? a.Nb : a.Lq_pad,
-                      pooled_ok ? a.Hkv : a.Hq, 64, 128, 1))
+  const void* pvsrc = pooled_ok ? (a.pv_conv != nullptr ? a.pv_conv : a.pv) : a.q;
+  if (!encode_tmap_3d(&m[4], pvsrc, pooled_ok && a.pv_conv != nullptr ? vdt : a.dt, a.D,
+                      pooled_ok ? a.Nb : a.Lq_pad, pooled_ok ? a.Hkv : a.Hq, 64, 128, 1))
     return false;
   return true;
 }
 
-cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, int* sched, cudaStream_t stream) {
-  if (attn_pair_supported(a)) return launch_attn_pair(a, L, sched, stream);
+namespace {
+
+// Byte layout of the split scratch inside the caller's workspace.
+struct SplitLayout {
+  int max_slots = 0, qcap = 0;
+  size_t flags = 0, entries = 0, recs = 0, parts = 0, clear = 0, total = 0;
+};
+
+SplitLayout split_layout(int max_slots, int Dt) {
+  auto up = [](size_t x, size_t al) { return (x + al - 1) / al * al; };
+  SplitLayout s;
+  s.max_slots = max_slots;
+  s.qcap = max_slots * (kMaxSeg - 1);
+  size_t off = 16;   // hdr: work counter, queue tail, queue head, (unused)
+  s.flags = off;
+  off = up(off + 4 * (size_t)s.qcap, 16);
+  s.entries = off;
+  off += 16 * (size_t)s.qcap;
+  s.recs = off;
+  off += 16 * (size_t)max_slots;
+  s.clear = off;     // everything before the partials is zeroed before each launch
+  s.parts = up(off, 256);
+  s.total = s.parts + 4 * (size_t)max_slots * kMaxSeg * (128 * Dt + 256);
+  return s;
+}
+
+int split_tile_width(const AttnArgs& a) { return a.D <= 64 ? 64 : 128; }
+
+}  // namespace
+
+size_t attn_tc_workspace_bytes(const AttnArgs& a) {
+  if (!attn_tc_supported(a) || attn_pair_supported(a)) return kAttnMinWorkspace;
+  const int nch = (a.G * a.tile_q) / 128;
+  const int items = a.Hkv * a.Nt * nch;
+  // the latest four tiles of every KV head (the dense tail and its neighbours)
+  const int slots = std::min(items, 4 * a.Hkv * nch);
+  if (slots <= 0) return kAttnMinWorkspace;
+  return std::max(split_layout(slots, split_tile_width(a)).total, (size_t)kAttnMinWorkspace);
+}
+
+namespace {
+
+cudaError_t launch_attn_tc_impl(const AttnArgs& a, const TcLaunch& L, void* workspace,
+                                int64_t workspace_bytes, cudaStream_t stream) {
   Params p;
   p.a = a;
   p.nch = (a.G * a.tile_q) / 128;
   p.items = a.Hkv * a.Nt * p.nch;
   const int fmt = a.dt == DT_BF16 ? 1 : 0;
+  const int vdt = a.vdt < 0 ? a.dt : a.vdt;
   p.idesc_qk = umma_idesc_f16(fmt, 128, 128, 0, 0);
-  p.idesc_pv = umma_idesc_f16(fmt, 128, a.D, 0, 1);
+  p.idesc_qk64 = umma_idesc_f16(fmt, 128, 64, 0, 0);
+  p.idesc_pv = umma_idesc_f16(vdt == DT_BF16 ? 1 : 0, 128, a.D, 0, 1);
+  int* sched = (workspace != nullptr && workspace_bytes >= (int64_t)sizeof(int))
+                   ? reinterpret_cast<int*>(workspace)
+                   : nullptr;
   p.sched = sched;
   p.status = L.status;
   p.budget = L.budget;
+  p.split = Split{};
   if (p.items == 0) return cudaSuccess;
+
+  // KV-segment split when the workspace holds the scratch for some slots.
+  SplitLayout sl;
+  if (sched != nullptr && reinterpret_cast<uintptr_t>(workspace) % 256 == 0) {
+    int slots = std::min(p.items, 4 * a.Hkv * p.nch);
+    while (slots > 0 && split_layout(slots, split_tile_width(a)).total > (size_t)workspace_bytes)
+      slots /= 2;
+    if (slots > 0) {
+      sl = split_layout(slots, split_tile_width(a));
+      char* base = reinterpret_cast<char*>(workspace);
+      p.split.hdr = reinterpret_cast<int*>(base);
+      p.split.flags = reinterpret_cast<int*>(base + sl.flags);
+      p.split.entries = reinterpret_cast<int4*>(base + sl.entries);
+      p.split.recs = reinterpret_cast<int4*>(base + sl.recs);
+      p.split.partials = reinterpret_cast<float*>(base + sl.parts);
+      p.split.max_slots = sl.max_slots;
+      p.split.qcap = sl.qcap;
+    }
+  }
 
   CUtensorMap m[6];
   if (!encode_attn_maps(a, m)) return cudaErrorInvalidValue;
   const int grid = max(1, min(L.num_sms, p.items));
   cudaError_t e = cudaSuccess;
   if (sched != nullptr) {
-    e = cudaMemsetAsync(sched, 0, sizeof(int), stream);
+    e = cudaMemsetAsync(sched, 0, p.split.max_slots > 0 ? sl.clear : sizeof(int), stream);
     if (e != cudaSuccess) return e;
   }
-#define FPV2_ATTN_LAUNCH(DD, TT)                                                            \
+  const int cgrid = std::max(1, std::min(p.split.max_slots, L.num_sms));
+  const bool gather = a.corr && a.pooled_dt != a.dt;   // float32 pooled K/V
+#define FPV2_ATTN_LAUNCH(DD, TT, VV, GG)                                                    \
   {                                                                                         \
     const size_t smem = smem_bytes<DD>();                                                   \
-    e = cudaFuncSetAttribute(attn_tc_kernel<DD, TT>,                                        \
+    e = cudaFuncSetAttribute(attn_tc_kernel<DD, TT, VV, GG>,                                \
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
     if (e != cudaSuccess) return e;                                                         \
-    attn_tc_kernel<DD, TT><<<grid, kThreads, smem, stream>>>(m[0], m[1], m[2], m[3], m[4], m[5], p);  \
+    attn_tc_kernel<DD, TT, VV, GG><<<grid, kThreads, smem, stream>>>(m[0], m[1], m[2], m[3], m[4], m[5], p); \
+    if (p.split.max_slots > 0) attn_combine_kernel<DD, TT><<<cgrid, 512, 0, stream>>>(p);    \
   }
-  if (a.D == 64 && a.dt == DT_BF16) FPV2_ATTN_LAUNCH(64, DT_BF16)
-  else if (a.D == 64 && a.dt == DT_F16) FPV2_ATTN_LAUNCH(64, DT_F16)
+#define FPV2_ATTN_TYPES(DD)                                                                 \
+  {                                                                                         \
+    if (a.dt == DT_BF16 && vdt == DT_F16) {                                                 \
+      if (gather) FPV2_ATTN_LAUNCH(DD, DT_BF16, DT_F16, true)                               \
+      else FPV2_ATTN_LAUNCH(DD, DT_BF16, DT_F16, false)                                     \
+    } else if (a.dt == DT_BF16 && vdt == DT_BF16) {                                         \
+      if (gather) FPV2_ATTN_LAUNCH(DD, DT_BF16, DT_BF16, true)                              \
+      else FPV2_ATTN_LAUNCH(DD, DT_BF16, DT_BF16, false)                                    \
+    } else if (a.dt == DT_F16 && vdt == DT_F16) {                                           \
+      if (gather) FPV2_ATTN_LAUNCH(DD, DT_F16, DT_F16, true)                                \
+      else FPV2_ATTN_LAUNCH(DD, DT_F16, DT_F16, false)                                      \
+    } else {                                                                                \
+      return cudaErrorInvalidValue;                                                         \
+    }                                                                                       \
+  }
+  if (a.D == 64) FPV2_ATTN_TYPES(64)
   // head_dim 96 runs on the 128-wide tiles: the tensor maps have the real
   // extent, so TMA fills columns 96..127 of Q/K/V with zeros (QK unchanged),
   // PV runs with N = 96, and the output store clips at column 96.
-  else if (a.D >= 96 && a.dt == DT_BF16) FPV2_ATTN_LAUNCH(128, DT_BF16)
-  else if (a.D >= 96 && a.dt == DT_F16) FPV2_ATTN_LAUNCH(128, DT_F16)
+  else if (a.D >= 96) FPV2_ATTN_TYPES(128)
   else return cudaErrorInvalidValue;
+#undef FPV2_ATTN_TYPES
 #undef FPV2_ATTN_LAUNCH
   return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, void* workspace,
+                           int64_t workspace_bytes, cudaStream_t stream) {
+  if (attn_pair_supported(a)) {
+    int* sched = (workspace != nullptr && workspace_bytes >= (int64_t)sizeof(int))
+                     ? reinterpret_cast<int*>(workspace)
+                     : nullptr;
+    return launch_attn_pair(a, L, sched, stream);
+  }
+  return launch_attn_tc_impl(a, L, workspace, workspace_bytes, stream);
 }
 
 }  // namespace fpv2

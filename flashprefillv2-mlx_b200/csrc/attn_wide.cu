@@ -32,7 +32,8 @@ constexpr int kBoxes = kD / 64;               // 64-column TMA boxes of a tile
 constexpr int kTile = 128 * kD * 2;           // 64 KB
 constexpr uint32_t kOCol = 0, kSCol = 256;    // O | S_0 | S_1
 
-template <int DT>
+// DT: input dtype; VT: operand type of the P.V product (V and P).
+template <int DT, int VT>
 __global__ void __launch_bounds__(kWThreads, 1)
     attn_wide_kernel(const __grid_constant__ CUtensorMap tmap_q,
                      const __grid_constant__ CUtensorMap tmap_k,
@@ -187,10 +188,13 @@ __global__ void __launch_bounds__(kWThreads, 1)
       } else {
         // Float32 pooled inputs: gather up to 64 listed entries in two parts --
         // rows e < 64 hold round(x), rows 64 + e hold round(x - round(x)) -- so
-        // the softmax can add the two score columns and P.V covers both parts;
-        // K first (its slot frees with the previous QK), then V (its slot frees
-        // with the previous PV, which is issued after this item's QK).
-        auto gather = [&](const void* src_base, uint32_t dst) {
+        // that Q.K^T accumulated over both parts carries the float32 pooled keys
+        // and P.V over both parts the float32 pooled values; K first (its slot
+        // frees with the previous QK), then V (its slot frees with the previous
+        // PV, which is issued after this item's QK).
+        // (values in the P.V operand type, scaled by 2^-v_exp[h] like the V copy)
+        const float vs = a.v_exp != nullptr ? ldexpf(1.f, -a.v_exp[ck.h]) : 1.f;
+        auto gather = [&](const void* src_base, uint32_t dst, bool is_v) {
           constexpr int kChunks = kD / 8;   // 16-byte chunks per row
           for (int idx = lane; idx < 128 * kChunks; idx += 32) {
             const int e = idx / kChunks, cidx = idx % kChunks;
@@ -204,8 +208,14 @@ __global__ void __launch_bounds__(kWThreads, 1)
               const long long src = ((long long)ck.h * a.Nb + blk) * kD + cidx * 8;
               const float4* f = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src_base) + src);
               const float4 x0 = __ldg(f), x1 = __ldg(f + 1);
-              val = make_uint4(pack2_split<DT>(x0.x, x0.y, low), pack2_split<DT>(x0.z, x0.w, low),
-                               pack2_split<DT>(x1.x, x1.y, low), pack2_split<DT>(x1.z, x1.w, low));
+              if (is_v)
+                val = make_uint4(pack2_split<VT>(x0.x * vs, x0.y * vs, low),
+                                 pack2_split<VT>(x0.z * vs, x0.w * vs, low),
+                                 pack2_split<VT>(x1.x * vs, x1.y * vs, low),
+                                 pack2_split<VT>(x1.z * vs, x1.w * vs, low));
+              else
+                val = make_uint4(pack2_split<DT>(x0.x, x0.y, low), pack2_split<DT>(x0.z, x0.w, low),
+                                 pack2_split<DT>(x1.x, x1.y, low), pack2_split<DT>(x1.z, x1.w, low));
             }
             asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst + off), "r"(val.x),
                          "r"(val.y), "r"(val.z), "r"(val.w)
@@ -217,13 +227,13 @@ __global__ void __launch_bounds__(kWThreads, 1)
         if (lane == 0) good = mbar_wait(smem_u32(k_empty), par, wc);
         good = __shfl_sync(0xffffffffu, good, 0);
         if (!good) return false;
-        gather(a.pk, k_smem);
+        gather(a.pk, k_smem, false);
         if (lane == 0) mbar_arrive(smem_u32(k_full));
         if (lane == 0) good = mbar_wait(smem_u32(v_empty), par, wc);
         good = __shfl_sync(0xffffffffu, good, 0);
         if (good) good = wait_stage();
         if (!good) return false;
-        gather(a.pv, v_smem);
+        gather(a.pv, v_smem, true);
         if (lane == 0) mbar_arrive(smem_u32(v_full));
       }
       ++kv;
@@ -294,6 +304,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
         r.nvalid = nvalid;
         r.flags = (emitted == 0 ? 1 : 0) | (emitted == n_items - 1 ? 2 : 0);
         r.w = w;
+        r.part = -1;
         r.mask[0] = r.mask[1] = r.mask[2] = r.mask[3] = 0u;
         ++emitted;
         return r;
@@ -339,6 +350,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
       Rec done;
       done.kind = KIND_DONE;
       done.kstart = done.nvalid = done.w = 0;
+      done.part = -1;
       done.flags = 3;
       done.mask[0] = done.mask[1] = done.mask[2] = done.mask[3] = 0u;
       Chunk none{};
@@ -361,7 +373,8 @@ __global__ void __launch_bounds__(kWThreads, 1)
       bool ok = true, need_ofree = false, first_pv = true, need_q = false;
       int prev = -1;   // kv index whose PV is pending
       bool prev_last = false;   // that PV closes its work item
-      auto issue_pv = [&](int n, bool last) -> bool {
+      bool prev_corr = false;   // that item is a gathered CORR item (high + low parts)
+      auto issue_pv = [&](int n, bool last, bool corr) -> bool {
         const int st = n & 1;
         if (!mbar_wait(smem_u32(v_full), n & 1, wc)) return false;
         if (!mbar_wait(smem_u32(&p_full[st]), (n >> 1) & 1, wc)) return false;
@@ -371,11 +384,14 @@ __global__ void __launch_bounds__(kWThreads, 1)
         }
         tc_fence_after();
         // O[128 x 256] += P V: P (128 keys as 16-bit pairs) in the first 64
-        // columns of the S buffer, V MN-major in four 64-column boxes.
+        // columns of the S buffer, V MN-major in four 64-column boxes. A CORR
+        // item's P (64 entries) multiplies the high value rows 0..63 and then the
+        // low value rows 64..127.
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t pcol = corr ? (uint32_t)(kk & 3) * 8 : (uint32_t)kk * 8;
           const uint64_t bdesc = sw128_desc(v_smem + kk * 2048, 16384, 1024);
-          umma_ts(tmem_base + kOCol, tmem_base + kSCol + st * 128 + kk * 8, bdesc, p.idesc_pv,
+          umma_ts(tmem_base + kOCol, tmem_base + kSCol + st * 128 + pcol, bdesc, p.idesc_pv,
                   (first_pv && kk == 0) ? 0u : 1u);
         }
         first_pv = false;
@@ -409,17 +425,33 @@ __global__ void __launch_bounds__(kWThreads, 1)
           if (!ok) break;
           tc_fence_after();
           const uint32_t s_tmem = tmem_base + kSCol + st * 128;
+          const bool corr = rec.kind == KIND_CORR;
+          if (!corr) {
 #pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk) {
-            const int hh = kk / 4, sub = kk % 4;
-            const uint64_t adesc = sw128_desc(q_smem + hh * 16384 + sub * 32, 16, 1024);
-            const uint64_t bdesc = sw128_desc(k_smem + hh * 16384 + sub * 32, 16, 1024);
-            umma_ss(s_tmem, adesc, bdesc, p.idesc_qk, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < kD / 16; ++kk) {
+              const int hh = kk / 4, sub = kk % 4;
+              const uint64_t adesc = sw128_desc(q_smem + hh * 16384 + sub * 32, 16, 1024);
+              const uint64_t bdesc = sw128_desc(k_smem + hh * 16384 + sub * 32, 16, 1024);
+              umma_ss(s_tmem, adesc, bdesc, p.idesc_qk, kk > 0 ? 1u : 0u);
+            }
+          } else {
+            // gathered CORR item: S[:, 0:64] = Q.K_high^T + Q.K_low^T (key rows 0..63
+            // and 64..127, 8 KB apart in each 64-column box), N = 64, one accumulator
+#pragma unroll
+            for (int part = 0; part < 2; ++part) {
+#pragma unroll
+              for (int kk = 0; kk < kD / 16; ++kk) {
+                const int hh = kk / 4, sub = kk % 4;
+                const uint64_t adesc = sw128_desc(q_smem + hh * 16384 + sub * 32, 16, 1024);
+                const uint64_t bdesc = sw128_desc(k_smem + hh * 16384 + part * 8192 + sub * 32, 16, 1024);
+                umma_ss(s_tmem, adesc, bdesc, p.idesc_qk64, (part | kk) ? 1u : 0u);
+              }
+            }
           }
           umma_commit(smem_u32(&s_full[st]));
           umma_commit(smem_u32(k_empty));
           if (rec.flags & 2) umma_commit(smem_u32(q_empty));   // Q no longer read
-          if (prev >= 0) ok = issue_pv(prev, prev_last);
+          if (prev >= 0) ok = issue_pv(prev, prev_last, prev_corr);
           if (!ok) break;
           if (rec.flags & 1) {
             need_ofree = wi > 0;
@@ -427,10 +459,11 @@ __global__ void __launch_bounds__(kWThreads, 1)
           }
           prev = kv;
           prev_last = (rec.flags & 2) != 0;
+          prev_corr = corr;
           ++kv;
         } else {
           // EMPTY work item: finish the pending PV, release Q, hand over an O of zeros.
-          if (prev >= 0) ok = issue_pv(prev, prev_last);
+          if (prev >= 0) ok = issue_pv(prev, prev_last, prev_corr);
           if (!ok) break;
           prev = -1;
           if (need_q) {
@@ -446,7 +479,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
           ++wi;
         }
       }
-      if (ok && prev >= 0) issue_pv(prev, prev_last);
+      if (ok && prev >= 0) issue_pv(prev, prev_last, prev_corr);
       umma_commit(smem_u32(drain));
       mbar_wait(smem_u32(drain), 0, wc, false);
     }
@@ -504,18 +537,6 @@ __global__ void __launch_bounds__(kWThreads, 1)
         reg_fence(s[1]);
         reg_fence(s[2]);
         reg_fence(s[3]);
-        if (rec.kind == KIND_CORR) {
-          // Key rows 64..127 of a gathered tile are the low parts of entries
-          // 0..63: s = S[:, j] + S[:, 64 + j], copied to both halves, so P.V
-          // multiplies the same P by the high and by the low parts.
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              s[c][j] = __float_as_uint(__uint_as_float(s[c][j]) + __uint_as_float(s[c + 2][j]));
-              s[c + 2][j] = s[c][j];
-            }
-        }
         // Validity of the 128 keys; a warp with any invalid entry masks on every lane.
         float bias = 0.f;
         uint32_t vm[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
@@ -537,13 +558,13 @@ __global__ void __launch_bounds__(kWThreads, 1)
           full = false;
 #pragma unroll
           for (int c = 0; c < 4; ++c) vm[c] = rec.mask[c];
-        } else {   // KIND_CORR: entries 0..63, duplicated in columns 64..127
+        } else {   // KIND_CORR (at most 64 entries)
           bias = a.corr_shift;
-          full = rec.nvalid >= 64;
+          full = rec.nvalid >= 128;
           if (!full) {
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
-              const int n = rec.nvalid - 32 * (c & 1);
+              const int n = rec.nvalid - 32 * c;
               vm[c] = n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
             }
           }
@@ -582,7 +603,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
           mt = full ? fmaf(m8, c2, bias) : m8;
         }
         const float m_new = fmaxf(m_used, mt);
-        const bool need = m_new > m_used + RescaleT<DT>::value ||
+        const bool need = m_new > m_used + RescaleT<VT>::value ||
                           (m_used == kFiniteMin && m_new > kFiniteMin);
         if (__any_sync(0xffffffffu, need)) {
           const float f = need ? ex2(m_used - m_new) : 1.f;
@@ -627,15 +648,11 @@ __global__ void __launch_bounds__(kWThreads, 1)
             pv.x = ex2(xv.x);
             pv.y = ex2(xv.y);
             rs[q & 3] = add_f32x2(rs[q & 3], pv);
-            if (c < 2) pk0[16 * c + q] = pack_p<DT>(pv.x, pv.y);
-            else pk1[16 * (c - 2) + q] = pack_p<DT>(pv.x, pv.y);
+            if (c < 2) pk0[16 * c + q] = pack_p<VT>(pv.x, pv.y);
+            else pk1[16 * (c - 2) + q] = pack_p<VT>(pv.x, pv.y);
           }
         }
-        {
-          // a CORR item's entries appear twice (high and low halves): count them once
-          const float sum = ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
-          l += rec.kind == KIND_CORR ? 0.5f * sum : sum;
-        }
+        l += ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
         // P of keys [0, 128) -> S columns [0, 64) (already read)
         tmem_st32(s_tmem, pk0);
         tmem_st32(s_tmem + 32, pk1);
@@ -670,7 +687,9 @@ __global__ void __launch_bounds__(kWThreads, 1)
       } else if (rec.flags & 2) {
         // ---- epilogue: out = O / l staged in the V buffer (the work item's
         // last PV has completed) as four 64-column TMA boxes, 128-byte swizzle.
-        const float inv = l > 0.f ? 1.f / l : 0.f;
+        // (times 2^v_exp[h] when V was scaled into the fp16 range)
+        const float vsc = a.v_exp != nullptr ? ldexpf(1.f, a.v_exp[ck.h]) : 1.f;
+        const float inv = l > 0.f ? vsc / l : 0.f;
         ok = mbar_wait(smem_u32(o_full), wi & 1, wc);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
@@ -786,8 +805,10 @@ cudaError_t launch_attn_wide(const AttnArgs& a, const TcLaunch& L, int* sched, c
   p.nch = (a.G * a.tile_q) / 128;
   p.items = a.Hkv * a.Nt * p.nch;
   const int fmt = a.dt == DT_BF16 ? 1 : 0;
+  const int vdt = a.vdt < 0 ? a.dt : a.vdt;
   p.idesc_qk = umma_idesc_f16(fmt, 128, 128, 0, 0);
-  p.idesc_pv = umma_idesc_f16(fmt, 128, kD, 0, 1);
+  p.idesc_qk64 = umma_idesc_f16(fmt, 128, 64, 0, 0);
+  p.idesc_pv = umma_idesc_f16(vdt == DT_BF16 ? 1 : 0, 128, kD, 0, 1);
   p.sched = sched;
   p.status = L.status;
   p.budget = L.budget;
@@ -802,13 +823,15 @@ cudaError_t launch_attn_wide(const AttnArgs& a, const TcLaunch& L, int* sched, c
                       box_rows, box_heads))
     return cudaErrorInvalidValue;
   if (!encode_tmap_3d(&tk, a.k, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return cudaErrorInvalidValue;
-  if (!encode_tmap_3d(&tv, a.v, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return cudaErrorInvalidValue;
+  if (!encode_tmap_3d(&tv, a.v_conv != nullptr ? a.v_conv : a.v, vdt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1))
+    return cudaErrorInvalidValue;
   const bool pooled_ok = a.corr && a.pooled_dt == a.dt;
   if (!encode_tmap_3d(&tpk, pooled_ok ? a.pk : a.k, a.dt, a.D, pooled_ok ? a.Nb : a.Lk_pad, a.Hkv,
                       64, 128, 1))
     return cudaErrorInvalidValue;
-  if (!encode_tmap_3d(&tpv, pooled_ok ? a.pv : a.v, a.dt, a.D, pooled_ok ? a.Nb : a.Lk_pad, a.Hkv,
-                      64, 128, 1))
+  const void* pvsrc = pooled_ok ? (a.pv_conv != nullptr ? a.pv_conv : a.pv)
+                                : (a.v_conv != nullptr ? a.v_conv : a.v);
+  if (!encode_tmap_3d(&tpv, pvsrc, vdt, a.D, pooled_ok ? a.Nb : a.Lk_pad, a.Hkv, 64, 128, 1))
     return cudaErrorInvalidValue;
   const int grid = max(1, min(L.num_sms, p.items));
   cudaError_t e = cudaSuccess;
@@ -817,17 +840,17 @@ cudaError_t launch_attn_wide(const AttnArgs& a, const TcLaunch& L, int* sched, c
     if (e != cudaSuccess) return e;
   }
   const size_t smem = wide_smem_bytes();
-  if (a.dt == DT_BF16) {
-    e = cudaFuncSetAttribute(attn_wide_kernel<DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
-    if (e != cudaSuccess) return e;
-    attn_wide_kernel<DT_BF16><<<grid, kWThreads, smem, stream>>>(tq, tk, tv, tpk, tpv, to, p);
-  } else {
-    e = cudaFuncSetAttribute(attn_wide_kernel<DT_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
-    if (e != cudaSuccess) return e;
-    attn_wide_kernel<DT_F16><<<grid, kWThreads, smem, stream>>>(tq, tk, tv, tpk, tpv, to, p);
+#define FPV2_WIDE_LAUNCH(TT, VV)                                                            \
+  {                                                                                         \
+    e = cudaFuncSetAttribute(attn_wide_kernel<TT, VV>,                                      \
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
+    if (e != cudaSuccess) return e;                                                         \
+    attn_wide_kernel<TT, VV><<<grid, kWThreads, smem, stream>>>(tq, tk, tv, tpk, tpv, to, p); \
   }
+  if (a.dt == DT_BF16 && vdt == DT_F16) FPV2_WIDE_LAUNCH(DT_BF16, DT_F16)
+  else if (a.dt == DT_BF16) FPV2_WIDE_LAUNCH(DT_BF16, DT_BF16)
+  else FPV2_WIDE_LAUNCH(DT_F16, DT_F16)
+#undef FPV2_WIDE_LAUNCH
   return cudaGetLastError();
 }
 

@@ -3,6 +3,7 @@
 // Each entry point checks its scalars and pointers, picks the tcgen05 kernel
 // when the shape fits it and the generic CUDA-core kernel otherwise, and
 // enqueues on the caller's stream. No host synchronisation, no allocation.
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -513,13 +514,47 @@ int run_sparse_attention(const void* q, const void* k, const void* v, const void
                        (!a.corr || (reinterpret_cast<uintptr_t>(pooled_k) % 16 == 0 &&
                                     reinterpret_cast<uintptr_t>(pooled_v) % 16 == 0));
   cudaError_t e;
-  if (aligned && attn_tc_supported(a)) {
-    int* sched = (workspace != nullptr && workspace_bytes >= (int64_t)sizeof(int))
-                     ? reinterpret_cast<int*>(workspace)
-                     : nullptr;
-    e = launch_attn_tc(a, tc_launch(*d), sched, s);
+  const bool use_tc = aligned && attn_tc_supported(a);
+  const bool use_wide = !use_tc && aligned && attn_wide_supported(a);
+  // bf16 inputs with room in the workspace: P.V in fp16 on an exact fp16 copy of V
+  // (the copy and its scratch lead the workspace; the rest serves the kernel).
+  if ((use_tc || use_wide) && dtype == DT_BF16 && workspace != nullptr &&
+      reinterpret_cast<uintptr_t>(workspace) % 256 == 0) {
+    const size_t conv = v_conv_bytes(kv_heads, padded_k_len, head_dim, a.Nb);
+    if (workspace_bytes >= (int64_t)(conv + kAttnMinWorkspace)) {
+      char* base = reinterpret_cast<char*>(workspace);
+      const size_t v_bytes = ((size_t)kv_heads * padded_k_len * head_dim * 2 + 255) / 256 * 256;
+      const size_t pv_bytes = ((size_t)kv_heads * a.Nb * head_dim * 2 + 255) / 256 * 256;
+      VConvArgs c;
+      c.v = v;
+      c.table = paged != nullptr ? paged->table : nullptr;
+      c.table_len = paged != nullptr ? paged->table_len : 0;
+      c.num_pages = paged != nullptr ? paged->num_pages : 0;
+      c.page_size = paged != nullptr ? paged->page_size : 0;
+      c.Hkv = kv_heads;
+      c.L = padded_k_len;
+      c.D = head_dim;
+      c.pv = (a.corr && pooled_dtype == dtype) ? pooled_v : nullptr;
+      c.Nb = a.Nb;
+      c.v16 = base;
+      c.pv16 = base + v_bytes;
+      c.v_exp = reinterpret_cast<int*>(base + v_bytes + pv_bytes);
+      c.absmax = reinterpret_cast<unsigned*>(c.v_exp + kv_heads);
+      e = launch_v_to_f16(c, s);
+      if (e != cudaSuccess) return cuda_fail(e, "V conversion launch");
+      a.vdt = DT_F16;
+      a.v_conv = c.v16;
+      a.pv_conv = c.pv != nullptr ? c.pv16 : nullptr;
+      a.v_exp = c.v_exp;
+      workspace = base + conv;
+      workspace_bytes -= (int64_t)conv;
+    }
+  }
+  if (use_tc) {
+    const bool ws_ok = workspace != nullptr && reinterpret_cast<uintptr_t>(workspace) % 4 == 0;
+    e = launch_attn_tc(a, tc_launch(*d), ws_ok ? workspace : nullptr, ws_ok ? workspace_bytes : 0, s);
     if (e != cudaSuccess) return cuda_fail(e, "attn_tc launch");
-  } else if (aligned && attn_wide_supported(a)) {
+  } else if (use_wide) {
     int* sched = (workspace != nullptr && workspace_bytes >= (int64_t)sizeof(int))
                      ? reinterpret_cast<int*>(workspace)
                      : nullptr;
@@ -558,6 +593,34 @@ int fpv2_sparse_attention(const void* q, const void* k, const void* v, const voi
                                     query_length, key_length, scale, block_k, tile_q,
                                     mean_correction, out, nullptr, 0, 0, workspace,
                                     workspace_bytes, stream);
+}
+
+int64_t fpv2_attention_workspace_bytes(int dtype, int32_t q_heads, int32_t kv_heads,
+                                       int32_t padded_q_len, int32_t padded_k_len,
+                                       int32_t head_dim, int32_t block_k, int32_t tile_q,
+                                       int pooled_dtype, int32_t mean_correction) {
+  if (kv_heads <= 0 || q_heads <= 0 || q_heads % kv_heads || tile_q <= 0 || block_k <= 0 ||
+      padded_q_len <= 0 || padded_k_len <= 0 || padded_q_len % tile_q || padded_k_len % block_k)
+    return FPV2_ATTN_WORKSPACE_BYTES;
+  AttnArgs a;
+  a.dt = dtype;
+  a.pooled_dt = pooled_dtype;
+  a.Hq = q_heads;
+  a.Hkv = kv_heads;
+  a.G = q_heads / kv_heads;
+  a.Lq_pad = padded_q_len;
+  a.Lk_pad = padded_k_len;
+  a.D = head_dim;
+  a.Nt = padded_q_len / tile_q;
+  a.Nb = padded_k_len / block_k;
+  a.block_k = block_k;
+  a.tile_q = tile_q;
+  a.corr = mean_correction ? 1 : 0;
+  a.scale_log2 = 1.f;
+  size_t bytes = attn_tc_workspace_bytes(a);
+  if (dtype == DT_BF16 && (attn_tc_supported(a) || attn_wide_supported(a)))
+    bytes += v_conv_bytes(kv_heads, padded_k_len, head_dim, a.Nb);   // fp16 copy of V
+  return (int64_t)std::max<size_t>(bytes, FPV2_ATTN_WORKSPACE_BYTES);
 }
 
 int fpv2_sparse_attention_multicast(

@@ -135,10 +135,11 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
 
 // 2^x for a pair, x <= 16, on the FMA and integer pipes instead of the MUFU:
 // n = rint(x) through the 1.5 * 2^23 rounding constant, f = x - n in
-// [-0.5, 0.5], 2^f by a quartic fitted (least maximum relative error) to
-// relative error < 2.7e-6 on that interval (checked in float32 over the whole
-// input range), and n added to the exponent field. Inputs below -126 are
-// clamped (the result is then below 2^-125).
+// [-0.5, 0.5], 2^f by the minimax quartic for relative error on that
+// interval (Remez exchange, levelled error 2.6e-6; tests/exp2_poly_fit.py
+// reproduces the coefficients, and the float32 evaluation is checked below
+// 2.7e-6 over the whole input range), and n added to the exponent field.
+// Inputs below -126 are clamped (the result is then below 2^-125).
 __device__ __forceinline__ float2 exp2_poly_x2(float2 x) {
   x.x = fmaxf(x.x, -126.f);
   x.y = fmaxf(x.y, -126.f);

@@ -87,7 +87,34 @@ struct AttnArgs {
   int page_size = 0;
   int num_pages = 0;
   int table_len = 0;
+  // Operand type of the P.V product (-1: the input dtype). For bf16 inputs the
+  // tcgen05 kernels can run P.V in fp16 -- P rounded to 11 significant bits
+  // instead of 8 -- on an exact fp16 copy of V: v_conv [Hkv, Lk_pad, D] and
+  // pooled_v_conv [Hkv, Nb, D] (contiguous even when k/v are paged), holding
+  // the values times 2^-v_exp[h] (v_exp: per KV head, null = 0); the output is
+  // scaled back by 2^v_exp[h].
+  int vdt = -1;
+  const void* v_conv = nullptr;
+  const void* pv_conv = nullptr;
+  const int* v_exp = nullptr;
 };
+
+// ---- V -> fp16 copy for the P.V product (convert.cu) -------------------------
+struct VConvArgs {
+  const void* v;                 // bf16 [Hkv, L, D], or a page pool [pages, page_size, Hkv, D]
+  const int32_t* table;          // page table (null: contiguous v)
+  int table_len, num_pages, page_size;
+  int Hkv, L, D;
+  const void* pv;                // pooled V bf16 [Hkv, Nb, D] (null: none)
+  int Nb;
+  void* v16;                     // out: fp16 [Hkv, L, D]
+  void* pv16;                    // out: fp16 [Hkv, Nb, D]
+  int* v_exp;                    // out: [Hkv] power-of-two exponent of the scaling
+  unsigned* absmax;              // scratch: [Hkv] (zeroed by the launcher)
+};
+cudaError_t launch_v_to_f16(const VConvArgs& a, cudaStream_t stream);
+// Bytes of the fp16 copies and their scratch (256-byte aligned pieces).
+size_t v_conv_bytes(int Hkv, int L, int D, int Nb);
 cudaError_t launch_attn_generic(const AttnArgs& a, cudaStream_t stream);
 
 // ---- tcgen05 kernels -------------------------------------------------------
@@ -118,7 +145,14 @@ cudaError_t launch_select_tc(const SelectTcArgs& a, const void* q, const void* p
 // `sched` (nullable) is one int of device scratch used as the work-queue
 // counter; it is zeroed on `stream` before the launch. Null = static schedule.
 bool attn_tc_supported(const AttnArgs& a);
-cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, int* sched, cudaStream_t stream);
+// `workspace` (nullable, `workspace_bytes` long): its first int is the
+// work-queue counter; a workspace of attn_tc_workspace_bytes(a) or more also
+// holds the scratch of the KV-segment split of long work items (the partial
+// results and their queue), which then runs; a smaller one runs without it.
+constexpr size_t kAttnMinWorkspace = 16;
+size_t attn_tc_workspace_bytes(const AttnArgs& a);
+cudaError_t launch_attn_tc(const AttnArgs& a, const TcLaunch& L, void* workspace,
+                           int64_t workspace_bytes, cudaStream_t stream);
 // attn_pair.cu: the same with two query chunks of a tile per K/V stream;
 // launch_attn_tc routes the shapes it supports (an even number of chunks per
 // tile that pair up at the same query positions) to it.

@@ -68,6 +68,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
          ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
          ctypes.c_int64, ctypes.c_void_p],
     ),
+    "fpv2_attention_workspace_bytes": (
+        ctypes.c_int64,
+        [ctypes.c_int, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int, ctypes.c_int32],
+    ),
     "fpv2_sparse_attention_multicast": (
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
@@ -188,6 +193,17 @@ def device_status(device: torch.device | int | None = None, clear: bool = True) 
         stream = torch.cuda.current_stream().cuda_stream
         check(lib().fpv2_device_status(stream, 1 if clear else 0, ctypes.byref(out)))
     return int(out.value)
+
+
+def attention_workspace(q: torch.Tensor, kv_heads: int, padded_k_len: int, block_k: int,
+                        tile_q: int, pooled_dtype: torch.dtype, mean_correction: bool) -> torch.Tensor:
+    """Device workspace for one attention call, sized by the library so that long
+    work items can be split over the GPU (``fpv2_attention_workspace_bytes``)."""
+    nbytes = lib().fpv2_attention_workspace_bytes(
+        dtype_code(q.dtype), q.shape[0], kv_heads, q.shape[1], padded_k_len, q.shape[2], block_k,
+        tile_q, dtype_code(pooled_dtype), 1 if mean_correction else 0)
+    return torch.empty((max(int(nbytes), ATTN_WORKSPACE_BYTES) + 3) // 4, dtype=torch.int32,
+                       device=q.device)
 
 
 def set_wait_budget_ms(milliseconds: float) -> None:

@@ -220,7 +220,8 @@ def sparse_attention(
     qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
     pkc, pvc = pooled_k.contiguous(), pooled_v.contiguous()
     lc = [x.contiguous() for x in (selected_ids, selected_counts, pruned_ids, pruned_counts)]
-    workspace = torch.empty(_lib.ATTN_WORKSPACE_BYTES // 4, dtype=torch.int32, device=q.device)
+    workspace = _lib.attention_workspace(qc, kv_heads, padded_key_length, config.block_k,
+                                         config.tile_q, pkc.dtype, config.mean_correction)
     args = (
         _lib.ptr(qc), _lib.ptr(kc), _lib.ptr(vc), _lib.ptr(pkc), _lib.ptr(pvc),
         _lib.dtype_code(pkc.dtype), _lib.ptr(lc[0]), _lib.ptr(lc[1]), _lib.ptr(lc[2]),

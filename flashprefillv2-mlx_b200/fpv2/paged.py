@@ -139,7 +139,8 @@ def sparse_attention_paged(
     qc, kc, vc, bt = q.contiguous(), k_cache.contiguous(), v_cache.contiguous(), block_table.contiguous()
     pkc, pvc = pooled_k.contiguous(), pooled_v.contiguous()
     lc = [x.contiguous() for x in (selected_ids, selected_counts, pruned_ids, pruned_counts)]
-    workspace = torch.empty(_lib.ATTN_WORKSPACE_BYTES // 4, dtype=torch.int32, device=q.device)
+    workspace = _lib.attention_workspace(qc, kv_heads, padded_key_length, config.block_k,
+                                         config.tile_q, pkc.dtype, config.mean_correction)
     out = torch.empty_like(qc)
     _lib.check(_lib.lib().fpv2_sparse_attention_paged(
         _lib.ptr(qc), _lib.ptr(kc), _lib.ptr(vc), _lib.ptr(bt), bt.numel(), num_pages, page_size,

@@ -108,6 +108,7 @@ def head_parallel_sdpa(
     config: FPV2Config = FPV2Config(),
     group=None,
     fused: bool | None = None,
+    copy: bool = True,
 ) -> torch.Tensor:
     """FPV2 on this rank's head shard (``[1, Hq/P, L, D]``, ``[1, Hkv/P, L, D]``);
     every rank returns the full ``[1, Hq, L, D]`` output.
@@ -115,9 +116,12 @@ def head_parallel_sdpa(
     Fused (the default where the GPUs support NVLink multicast): the attention
     kernel writes each finished output tile straight into every rank's copy of
     the full output through the multicast address (torch symmetric memory), so
-    the reassembly overlaps the computation; the returned tensor is a view of
-    that shared buffer, valid until the next call with the same shape. Otherwise
-    one NCCL all-gather follows the kernel."""
+    the reassembly overlaps the computation. That buffer is cached per shape and
+    reused by the next call of the same shape (every layer of a model), so by
+    default the result is copied out of it; ``copy=False`` returns the buffer
+    itself, valid only until the next call with the same shape (for callers that
+    consume the output before the next layer). Otherwise one NCCL all-gather
+    follows the kernel and the result is a fresh tensor either way."""
     from fpv2 import _lib
     from fpv2.patch import _effective_config
 
@@ -140,7 +144,8 @@ def head_parallel_sdpa(
     handle.barrier(channel=0)   # no rank still reads the previous contents
     fpv2_sdpa(q, k, v, scale=scale, config=config, multicast=(mc_addr, rank * hq, world * hq))
     handle.barrier(channel=0)   # every rank's tiles have landed in every buffer
-    return buf[None, :, :lq, :]
+    out = buf[None, :, :lq, :]
+    return out.clone() if copy else out
 
 
 class RankMonitor:

@@ -139,7 +139,13 @@ FPV2_API int fpv2_index_stage(const void* q, const void* k, const void* v, int d
  * `workspace` (nullable) is caller-owned device scratch of at least
  * FPV2_ATTN_WORKSPACE_BYTES: the kernel's work-queue counter, rewritten on
  * `stream` by every call (calls sharing one workspace must be stream-ordered).
- * Without it the work is distributed statically (same results, slower).
+ * Without it the work is distributed statically (same results, slower). A
+ * 256-byte aligned workspace of fpv2_attention_workspace_bytes() bytes also
+ * holds, for bf16 inputs, an exact fp16 copy of V so that P is held at fp16
+ * precision in the P.V product (11 significant bits instead of bf16's 8), and
+ * the partial results of long work items, which are then split into segments
+ * over the GPU; smaller workspaces run without either (results within the
+ * same output tolerance, slightly less precise).
  * Replaces fpv2/kernel.py:441-590 (sparse_attention) and its Metal kernel
  * fpv2/kernel.py:187-414.
  */
@@ -154,6 +160,21 @@ FPV2_API int fpv2_sparse_attention(const void* q, const void* k, const void* v, 
                           int32_t block_k, int32_t tile_q, int32_t mean_correction,
                           void* out, void* workspace, int64_t workspace_bytes,
                           void* stream);
+
+/*
+ * Workspace size for fpv2_sparse_attention / _multicast / _paged that enables
+ * (a) for bf16 inputs, the fp16 P.V product on an exact fp16 copy of V (the
+ * reference multiplies a float32 P by V upcast to float32, fpv2/kernel.py:
+ * 234-235, 322; fp16 P comes 8x closer to that than bf16 P), and (b) the split
+ * of long work items (the dense-tail tiles that walk every key block) into
+ * segments spread over the SMs. Any smaller workspace of at least
+ * FPV2_ATTN_WORKSPACE_BYTES runs without them. Never smaller than
+ * FPV2_ATTN_WORKSPACE_BYTES. No counterpart in the reference.
+ */
+FPV2_API int64_t fpv2_attention_workspace_bytes(int dtype, int32_t q_heads, int32_t kv_heads,
+                                       int32_t padded_q_len, int32_t padded_k_len,
+                                       int32_t head_dim, int32_t block_k, int32_t tile_q,
+                                       int pooled_dtype, int32_t mean_correction);
 
 /*
  * fpv2_sparse_attention for the head-parallel multi-GPU layer, with the output

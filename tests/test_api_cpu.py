@@ -24,7 +24,7 @@ ROOT = Path(__file__).resolve().parents[1]
 
 def declared_symbols() -> list[str]:
     header = (ROOT / "include" / "fpv2_b200.h").read_text()
-    return re.findall(r"FPV2_API\s+(?:const\s+char\s*\*|int)\s+(fpv2_\w+)\s*\(", header)
+    return re.findall(r"FPV2_API\s+(?:const\s+char\s*\*|int64_t|int)\s+(fpv2_\w+)\s*\(", header)
 
 
 def test_library_exports_every_declared_symbol():

@@ -67,3 +67,15 @@ def test_exp2_poly_clamps_without_sign_or_exponent_wrap():
     x = np.array([-1e30, -3.0e38, -200.0, -127.0, -126.0], dtype=np.float32)
     got = _poly_exp2(x, coeffs)
     assert np.all(got >= 0.0) and np.all(got < 2.0 ** -124)
+
+
+def test_coefficients_are_the_minimax_relative_error_fit():
+    """The shipped coefficients are the Remez (minimax relative error) quartic for
+    2^f on [-0.5, 0.5] (tests/exp2_poly_fit.py), to float32-level agreement."""
+    from tests.exp2_poly_fit import float32_coefficients, remez_exp2
+
+    _, levelled = remez_exp2()
+    assert levelled < 2.7e-6
+    fitted = np.array(float32_coefficients())
+    shipped = np.array(_coefficients())
+    assert np.allclose(fitted, shipped, rtol=2e-5, atol=0.0), (fitted, shipped)

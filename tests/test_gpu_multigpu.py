@@ -64,8 +64,16 @@ def _worker(rank: int, world: int, port: int, length: int, hq: int, hkv: int, d:
             torch.cuda.synchronize(dev)
             diff = (out.float() - ref.float()).abs().max().item()
             report.append(f"{diff}")
+        # a kept output is the caller's own: the next same-shape call (different
+        # values) must not overwrite it, while copy=False aliases the shared buffer
+        kept = out
+        other = head_parallel_sdpa(ql, kl, 2 * vl, scale=d ** -0.5, config=cfg, fused=True,
+                                   copy=False)
+        torch.cuda.synchronize(dev)
+        report.append(f"{(kept.float() - ref.float()).abs().max().item()}")
+        aliased = other.data_ptr() != kept.data_ptr()
         multicast = any(e is not None for e in _SYMM_BUFFERS.values())
-        queue.put((rank, f"maxdiff {' '.join(report)} multicast {multicast}"))
+        queue.put((rank, f"maxdiff {' '.join(report)} multicast {multicast} distinct {aliased}"))
         dist.barrier()
         dist.destroy_process_group()
     except Exception:  # pragma: no cover - reported to the parent
@@ -92,4 +100,5 @@ def test_head_parallel_two_gpus_matches_single_gpu(length, hq, hkv, d):
     alive = [p.pid for p in procs if p.is_alive()]
     assert not alive, f"ranks still running after 120 s (pids {alive})"
     for rank in (0, 1):
-        assert results[rank].startswith("maxdiff 0.0 0.0 0.0 multicast"), results[rank]
+        assert results[rank].startswith("maxdiff 0.0 0.0 0.0 0.0 multicast"), results[rank]
+        assert results[rank].endswith("distinct True"), results[rank]

@@ -403,3 +403,85 @@ def test_bounded_wait_times_out_and_context_survives():
     x = torch.ones(4, device=DEV)
     assert x.sum().item() == 4.0   # context still usable
     assert _lib.device_status() == 0
+
+
+# ---------------------------------------------------------------------------
+# workspace-dependent paths: fp16 copy of V, KV-segment split of long items
+# ---------------------------------------------------------------------------
+
+
+def _attention_with_workspace(q, k, v, pk, pv, lists, cfg, scale, nbytes):
+    """fpv2_sparse_attention through the C ABI with a workspace of ``nbytes``."""
+    import ctypes
+
+    out = torch.full_like(q, float("nan"))
+    ws = torch.zeros((max(nbytes, 16) + 3) // 4, dtype=torch.int32, device=q.device)
+    rc = _lib.lib().fpv2_sparse_attention(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), pk.data_ptr(), pv.data_ptr(),
+        _lib.dtype_code(pk.dtype), lists[0].data_ptr(), lists[1].data_ptr(), lists[2].data_ptr(),
+        lists[3].data_ptr(), _lib.dtype_code(q.dtype), q.shape[0], k.shape[0], q.shape[1],
+        k.shape[1], q.shape[2], 0, q.shape[1], k.shape[1], ctypes.c_float(scale), cfg.block_k,
+        cfg.tile_q, 1 if cfg.mean_correction else 0, out.data_ptr(), ws.data_ptr(),
+        ws.numel() * 4, torch.cuda.current_stream().cuda_stream)
+    assert rc == _lib.OK, _lib.lib().fpv2_last_error().decode()
+    return out
+
+
+def test_long_items_split_over_segments():
+    """At 32k the dense-tail tiles walk 256 key blocks: with the full workspace they
+    are split into segments whose partial results a combine kernel merges. The
+    split layer agrees with the unsplit one (same fp16 product, workspace without
+    the split scratch) to within rounding, and with the float32 math."""
+    length, hq, hkv = 32768, 8, 2
+    q, k, v = topic_qkv(length=length, query_heads=hq, kv_heads=hkv, seed=61, dtype=torch.bfloat16)
+    cfg = _effective_config(fpv2.FPV2Config(alpha=0.1), hq, hkv)
+    scale = 128 ** -0.5
+    qg, kg, vg = cuda(q, k, v)
+    pk, pv, lists, mask = fpv2.index_stage(qg, kg, vg, scale=scale, config=cfg, offset=0,
+                                           query_length=length, key_length=length, return_mask=True)
+    full = _lib.lib().fpv2_attention_workspace_bytes(
+        _lib.BF16, hq, hkv, length, length, 128, 128, cfg.tile_q, _lib.BF16, 1)
+    nt = length // cfg.tile_q
+    split = _attention_with_workspace(qg, kg, vg, pk, pv, lists, cfg, scale, full)
+    default = fpv2.sparse_attention(qg, kg, vg, pk, pv, *lists, scale=scale, config=cfg)
+    assert torch.equal(split, default)   # the Python operator sizes its workspace the same way
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    nb = length // 128
+    v_copy = ((hkv * length * 128 * 2 + 255) // 256 * 256 + (hkv * nb * 128 * 2 + 255) // 256 * 256
+              + (hkv * 8 + 255) // 256 * 256)
+    unsplit = _attention_with_workspace(qg, kg, vg, pk, pv, lists, cfg, scale, v_copy + 4096)
+    mx, mean = P.kernel_errors(split, P.np32(unsplit))
+    assert mx <= 2 ** -7 and mean <= 1e-5, (mx, mean)
+    tiles = [0, nt // 2, nt - 3, nt - 2, nt - 1]
+    ref = O.fpv2_attention_blockwise(P.np32(q), P.np32(k), P.np32(v), scale=scale, config=cfg,
+                                     selected=mask.cpu().numpy(), pooled_dtype="bf16",
+                                     tiles=[(h, t) for h in range(hkv) for t in tiles])
+    pos = P.tile_positions(tiles, cfg.tile_q, length)
+    err = np.abs(P.rows_of(split, pos) - ref[:, pos])
+    assert err.max() <= P.MAX_ABS_TOL and err.mean() <= P.MEAN_ABS_TOL, (err.max(), err.mean())
+
+
+def test_v_beyond_fp16_range_is_rescaled():
+    """bf16 values beyond the fp16 range: the fp16 copy of V is scaled by a power of
+    two per KV head and the output scaled back, so scaling V by 2^17 scales the
+    output by 2^17 (exactly, up to the few values that the unscaled copy holds
+    as fp16 subnormals)."""
+    q, k, v = topic_qkv(length=4096, query_heads=8, kv_heads=2, seed=62, dtype=torch.bfloat16)
+    cfg = _effective_config(fpv2.FPV2Config(alpha=0.1), 8, 2)
+    scale = 128 ** -0.5
+    qg, kg, vg = cuda(q, k, v)
+    big = vg * (2.0 ** 17)
+    assert big.float().abs().max().item() > 65504.0
+    pk, pv, lists, _ = fpv2.index_stage(qg, kg, vg, scale=scale, config=cfg, offset=0,
+                                        query_length=4096, key_length=4096)
+    pkb, pvb, listsb, _ = fpv2.index_stage(qg, kg, big, scale=scale, config=cfg, offset=0,
+                                           query_length=4096, key_length=4096)
+    assert all(torch.equal(x, y) for x, y in zip(lists, listsb))
+    out = fpv2.sparse_attention(qg, kg, vg, pk, pv, *lists, scale=scale, config=cfg)
+    outb = fpv2.sparse_attention(qg, kg, big, pkb, pvb, *listsb, scale=scale, config=cfg)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    assert torch.isfinite(outb).all()
+    mx, mean = P.kernel_errors(outb / (2.0 ** 17), P.np32(out))
+    assert mx <= 2 ** -7 and mean <= 1e-6, (mx, mean)

@@ -8,10 +8,13 @@ attention kernel's work-queue counter in a fixed array inside the library
 instead of a caller-provided workspace.
 
 The GPU test calls it through the C ABI twice in a row on the same inputs and
-checks each output against the regular entry point, ``fpv2_sparse_attention``
-with a caller workspace: the same kernel on the same lists, so the outputs must
-be bit-identical (every work item is computed whole by one CTA, whatever order
-the CTAs take the items in). The cases reach all three tensor-core attention
+checks each output against the regular entry point, ``fpv2_sparse_attention``,
+given a caller workspace of the same size as the library's array
+(FPV2_NOALLOC_SCRATCH_BYTES: room for the work counter only, so neither runs
+the fp16 copy of V nor the split of long work items that a full workspace
+enables): the same kernel on the same lists, so the outputs must be
+bit-identical (every work item is computed whole by one CTA, whatever order the
+CTAs take the items in). The cases reach all three tensor-core attention
 kernels that draw work from the counter: the single-chunk kernel (default
 tiles), the chunk-pair kernel (128-position tiles, four 128-row chunks per
 tile) and the head_dim 256 kernel. This file is collected last on purpose, and
@@ -22,6 +25,7 @@ from __future__ import annotations
 
 import ctypes
 from dataclasses import replace
+from pathlib import Path
 
 import pytest
 import torch
@@ -40,6 +44,24 @@ def _noalloc(q, k, v, pk, pv, lists, out, cfg, scale, stream):
         k.shape[0], q.shape[1], k.shape[1], q.shape[2], 0, q.shape[1], k.shape[1],
         ctypes.c_float(scale), cfg.block_k, cfg.tile_q, 1 if cfg.mean_correction else 0,
         out.data_ptr(), stream)
+
+
+NOALLOC_SCRATCH_BYTES = 256   # FPV2_NOALLOC_SCRATCH_BYTES (include/fpv2_b200.h)
+
+
+def _workspace_call(q, k, v, pk, pv, lists, out, cfg, scale, ws, stream):
+    return _lib.lib().fpv2_sparse_attention(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), pk.data_ptr(), pv.data_ptr(),
+        _lib.dtype_code(pk.dtype), lists[0].data_ptr(), lists[1].data_ptr(),
+        lists[2].data_ptr(), lists[3].data_ptr(), _lib.dtype_code(q.dtype), q.shape[0],
+        k.shape[0], q.shape[1], k.shape[1], q.shape[2], 0, q.shape[1], k.shape[1],
+        ctypes.c_float(scale), cfg.block_k, cfg.tile_q, 1 if cfg.mean_correction else 0,
+        out.data_ptr(), ws.data_ptr(), ws.numel() * 4, stream)
+
+
+def test_noalloc_scratch_size_matches_header():
+    header = (Path(__file__).resolve().parents[1] / "include" / "fpv2_b200.h").read_text()
+    assert f"#define FPV2_NOALLOC_SCRATCH_BYTES {NOALLOC_SCRATCH_BYTES}" in header
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch():
@@ -68,8 +90,11 @@ def test_noalloc_matches_workspace_entry_twice(length, hq, hkv, head_dim, tile_q
     scale = head_dim ** -0.5
     pk, pv, lists, _ = fpv2.index_stage(q, k, v, scale=scale, config=cfg, offset=0,
                                         query_length=length, key_length=length)
-    expected = fpv2.sparse_attention(q, k, v, pk, pv, *lists, scale=scale, config=cfg)
     stream = torch.cuda.current_stream(dev).cuda_stream
+    expected = torch.full_like(q, float("nan"))
+    ws = torch.zeros(NOALLOC_SCRATCH_BYTES // 4, dtype=torch.int32, device=dev)
+    rc = _workspace_call(q, k, v, pk, pv, lists, expected, cfg, scale, ws, stream)
+    assert rc == _lib.OK, _lib.lib().fpv2_last_error().decode()
     for _ in range(2):
         out = torch.full_like(q, float("nan"))
         rc = _noalloc(q, k, v, pk, pv, lists, out, cfg, scale, stream)
