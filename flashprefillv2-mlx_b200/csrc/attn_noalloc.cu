@@ -17,7 +17,11 @@
 //   example on two streams) race on it;
 // * the first call on a device looks up the array's device address
 //   (cudaGetSymbolAddress with that device current); make that first call
-//   before any stream capture.
+//   before any stream capture. The address is cached for the life of the
+//   process, so the library must not be used across a cudaDeviceReset of that
+//   device (the array is re-created at a new address);
+// * with only this scratch the call runs without the fp16 copy of V and the
+//   split of long work items that a full caller workspace enables.
 #include <mutex>
 
 #include "../../include/fpv2_b200.h"

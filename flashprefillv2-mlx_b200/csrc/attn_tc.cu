@@ -228,6 +228,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           w = __shfl_sync(0xffffffffu, e.x, 0);
           seg = __shfl_sync(0xffffffffu, e.y, 0);
           nseg = __shfl_sync(0xffffffffu, e.z, 0);
+          if (w < 0 || w >= p.split.max_slots || w >= p.items || nseg < 2 || nseg > kMaxSeg ||
+              seg < 1 || seg >= nseg) {   // entry failed its bounds check: report, stop
+            if (lane == 0) {
+              atomicOr(wc.status, STATUS_BAD_SPLIT);
+              *wc.abort_flag = 1;
+            }
+            ok = false;
+            return false;
+          }
           return true;
         }
       }
@@ -405,15 +414,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       // segments 1.. for the other CTAs (this CTA runs segment 0).
       if (split && nseg == 0 && w < p.split.max_slots && n_total > 2 * kSegLen) {
         const int want = min(kMaxSeg, (n_total + kSegLen - 1) / kSegLen);
+        int pushed = 1;
         if (lane == 0) {
-          p.split.recs[w] = make_int4(w, want, 0, 0);
           const int base = atomicAdd(&p.split.hdr[1], want - 1);
-          for (int s2 = 1; s2 < want; ++s2)
-            p.split.entries[base + s2 - 1] = make_int4(w, s2, want, 0);
-          __threadfence();
-          for (int s2 = 1; s2 < want; ++s2) atomicExch(&p.split.flags[base + s2 - 1], 1);
+          if (base < 0 || base + want - 1 > p.split.qcap) {   // cannot happen: qcap covers every slot
+            atomicOr(wc.status, STATUS_BAD_SPLIT);
+            pushed = 0;
+          } else {
+            p.split.recs[w] = make_int4(w, want, 0, 0);
+            for (int s2 = 1; s2 < want; ++s2)
+              p.split.entries[base + s2 - 1] = make_int4(w, s2, want, 0);
+            __threadfence();
+            for (int s2 = 1; s2 < want; ++s2) atomicExch(&p.split.flags[base + s2 - 1], 1);
+          }
         }
-        nseg = want;
+        pushed = __shfl_sync(0xffffffffu, pushed, 0);
+        nseg = pushed ? want : 0;
       }
       // This unit's share [lo, hi) of the item's KV item sequence.
       int lo = 0, hi = n_total, part = -1;
@@ -828,7 +844,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int qs = wi & 1;
         const uint32_t stage = q_smem + qs * C::kTileBytes;
         const uint32_t o0 = tmem_base + lane_off + C::kOCol + half * (D / 2);
-        float* part = rec.part >= 0 ? p.split.partials + (size_t)rec.part * (128 * D + 256) : nullptr;
+        float* part = nullptr;
+        if (rec.part >= 0) {
+          if (p.split.partials != nullptr && rec.part < p.split.max_slots * kMaxSeg)
+            part = p.split.partials + (size_t)rec.part * (128 * D + 256);
+          else if (lane == 0)
+            atomicOr(p.status, STATUS_BAD_SPLIT);   // bounds check failed: the slot is skipped
+        }
 #pragma unroll 1
         for (int dc = 0; dc < D / 64; ++dc) {
           uint32_t x0[32], x1[32];
@@ -969,6 +991,10 @@ __global__ void __launch_bounds__(512) attn_combine_kernel(Params p) {
     const int4 rec = p.split.recs[slot];
     const int nseg = min(rec.y, kMaxSeg);
     if (nseg <= 0) continue;
+    if (rec.x != slot || rec.x >= p.items) {   // bounds check failed: report, skip the slot
+      if (threadIdx.x == 0) atomicOr(p.status, STATUS_BAD_SPLIT);
+      continue;
+    }
     const Chunk ck = make_chunk(p, rec.x);
     const float* base = p.split.partials + (size_t)slot * kMaxSeg * kPart;
     for (int idx = threadIdx.x; idx < 128 * kGroups; idx += blockDim.x) {

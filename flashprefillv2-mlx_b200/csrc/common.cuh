@@ -21,6 +21,7 @@ enum : int { DT_F16 = 0, DT_BF16 = 1, DT_F32 = 2 };
 enum : int {
   STATUS_TIMEOUT = 1,      // a bounded wait expired
   STATUS_TMEM_ALLOC = 2,   // TMEM allocation returned an unusable address
+  STATUS_BAD_SPLIT = 4,    // a split-queue entry or partial slot failed its bounds check
 };
 
 constexpr float kFiniteMin = -3.402823466e+38f;  // Metal's Limits<float>::finite_min

@@ -73,6 +73,13 @@ def sdpa_from_host(
             for t in (qb, kb, vb):
                 t.record_stream(h2d)
             bufs.append((qb, kb, vb))
+    # The buffers come from the compute stream's pool, which only orders their
+    # reuse with the compute stream: blocks still read by kernels queued there
+    # (the previous call's lists, scratch, inputs) may be handed out again. The
+    # copy stream starts after the compute stream's queued work for that reason.
+    ready = torch.cuda.Event()
+    ready.record(compute)
+    h2d.wait_event(ready)
     inputs_free: list[torch.cuda.Event | None] = [None, None]
     last = None
     for c in range(nchunks):

@@ -200,13 +200,18 @@ FPV2_API int fpv2_sparse_attention_multicast(
 
 /*
  * fpv2_sparse_attention for callers that cannot allocate device memory (no
- * counterpart in the reference). Same arguments and results as
- * fpv2_sparse_attention without the workspace: the kernel's work-queue counter
+ * counterpart in the reference). Same arguments as fpv2_sparse_attention
+ * without the workspace, and the results that call gives with a workspace of
+ * FPV2_NOALLOC_SCRATCH_BYTES: the kernel's work-queue counter
  * lives in a FPV2_NOALLOC_SCRATCH_BYTES array compiled into the library, held
  * by every GPU that loads it until exit. Every call on a device shares that
  * array (it is cleared on `stream` before each launch), so calls that overlap
  * on the GPU race. The first call on a device looks up the array's address;
- * make it before any stream capture. Problems with more than
+ * make it before any stream capture, and do not use the library across a
+ * cudaDeviceReset of that device (the cached address would be stale). The
+ * scratch holds no fp16 copy of V and no split results (see
+ * fpv2_attention_workspace_bytes), so bf16 inputs keep P in bf16 here; the
+ * output stays within the same tolerance. Problems with more than
  * FPV2_NOALLOC_MAX_WORK_ITEMS work items (128-row chunks of selection tiles)
  * are rejected with FPV2_ERR_INVALID_ARGUMENT.
  */

@@ -29,3 +29,23 @@ def test_sdpa_from_host_equals_device_layer(chunk, query_length):
     torch.cuda.synchronize(dev)
     assert out.is_pinned()
     assert torch.equal(out, ref.cpu())
+
+
+def test_back_to_back_calls_from_host():
+    """Calls queued back to back (no synchronisation between them) at a length
+    whose dense-tail tiles split over segments: each call's buffers come from the
+    compute stream's pool while the previous call's kernels may still run, so the
+    copies must wait for them. Every output equals the device layer."""
+    dev = torch.device("cuda", 0)
+    q, k, v = topic_qkv(length=32768, query_heads=8, kv_heads=2, seed=33, dtype=torch.bfloat16)
+    q, k, v = q[None], k[None], v[None]
+    cfg = fpv2.FPV2Config(alpha=0.1)
+    ref = fpv2.fpv2_sdpa(q.to(dev), k.to(dev), v.to(dev), scale=128 ** -0.5, config=cfg).cpu()
+    qh, kh, vh = (t.pin_memory() for t in (q, k, v))
+    outs = [fpv2.sdpa_from_host(qh, kh, vh, scale=128 ** -0.5, config=cfg) for _ in range(4)]
+    torch.cuda.synchronize(dev)
+    from fpv2 import _lib
+
+    assert _lib.device_status(dev) == 0
+    for out in outs:
+        assert torch.equal(out, ref)
