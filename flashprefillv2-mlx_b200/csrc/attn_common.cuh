@@ -33,24 +33,24 @@ struct Rec {
   uint32_t mask[4];   // POOL: entry e is a pruned block when bit (e & 31) of mask[e >> 5]
 };
 
-// KV-segment split of long work items (attn_tc_kernel). A work item w <
-// max_slots whose KV item count exceeds 2 * seg_len is cut into nseg <= kMaxSeg
-// contiguous segments of its KV item sequence: the CTA that takes the item
-// queues segments 1.. for the other CTAs and runs segment 0; every segment
-// writes its unnormalised output with its row maxima and sums, and
-// attn_combine_kernel merges them. Slots are the item indices themselves, so
-// which items split does not depend on timing.
+// KV-segment split of long work items (attn_tc_kernel). The work counter first
+// walks kMaxSeg units (w, s) for each of the first max_slots work items (the
+// latest tiles, whose causal extent is largest) and then the remaining items
+// one unit each. An item with more than 2 * kSegLen KV items is cut into
+// nseg = min(kMaxSeg, ceil(n / kSegLen)) contiguous segments of its KV item
+// sequence; unit (w, s < nseg) runs segment s and writes its unnormalised
+// output with its row maxima and sums to slot w * kMaxSeg + s, and
+// attn_combine_kernel merges the segments. Units that an item does not need
+// (s >= nseg, or s > 0 for a short item, which unit (w, 0) runs whole) are
+// skipped after the item's list walk. Which items split depends only on the
+// lists, never on timing.
 constexpr int kMaxSeg = 16;
 constexpr int kSegLen = 64;     // target KV items per segment
 
 struct Split {
-  int* hdr;            // [0] work counter, [1] queue tail, [2] queue head
-  int* flags;          // [qcap] queue entry written (zeroed before launch)
-  int4* entries;       // [qcap] (w, segment, nseg, 0)
   int4* recs;          // [max_slots] (w, nseg, 0, 0); nseg 0 = not split (zeroed before launch)
   float* partials;     // [max_slots][kMaxSeg][128 * Dt + 256]: O rows, then m[128], l[128]
   int max_slots;       // 0: no split
-  int qcap;
 };
 
 

@@ -180,71 +180,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       return w;
     };
-    // Next work unit: a queued segment of a split item first, else the next
-    // work item (seg 0, nseg 0 = not decided yet). False when no work is left.
-    auto next_unit = [&](int& w, int& seg, int& nseg) -> bool {
-      if (split) {
-        int got = -1;
-        if (lane == 0) {
-          // lock-free pop: every failed CAS means another CTA took an entry
-          while (true) {
-            const int tail = atomicAdd(&p.split.hdr[1], 0);
-            const int head = atomicAdd(&p.split.hdr[2], 0);
-            if (head >= tail) break;
-            if (atomicCAS(&p.split.hdr[2], head, head + 1) == head) {
-              got = head;
-              break;
-            }
-          }
-        }
-        got = __shfl_sync(0xffffffffu, got, 0);
-        if (got >= 0) {
-          int4 e = make_int4(0, 0, 0, 0);
-          bool good = true;
-          if (lane == 0) {
-            // the pusher reserved the entry before writing it: bounded wait for its flag
-            const volatile int* f = p.split.flags + got;
-            const long long t0 = clock64();
-            while (*f == 0) {
-              if (*wc.abort_flag) { good = false; break; }
-              if (clock64() - t0 > wc.budget) {
-                atomicOr(wc.status, STATUS_TIMEOUT);
-                *wc.abort_flag = 1;
-                good = false;
-                break;
-              }
-            }
-            if (good) {
-              __threadfence();
-              const volatile int* ev = reinterpret_cast<const volatile int*>(p.split.entries + got);
-              e = make_int4(ev[0], ev[1], ev[2], ev[3]);
-            }
-          }
-          good = __shfl_sync(0xffffffffu, good, 0);
-          if (!good) {
-            ok = false;
-            return false;
-          }
-          w = __shfl_sync(0xffffffffu, e.x, 0);
-          seg = __shfl_sync(0xffffffffu, e.y, 0);
-          nseg = __shfl_sync(0xffffffffu, e.z, 0);
-          if (w < 0 || w >= p.split.max_slots || w >= p.items || nseg < 2 || nseg > kMaxSeg ||
-              seg < 1 || seg >= nseg) {   // entry failed its bounds check: report, stop
-            if (lane == 0) {
-              atomicOr(wc.status, STATUS_BAD_SPLIT);
-              *wc.abort_flag = 1;
-            }
-            ok = false;
-            return false;
-          }
-          return true;
-        }
-      }
-      w = next_work();
-      seg = 0;
-      nseg = 0;
-      return w < p.items;
-    };
+    // Units: kMaxSeg per item of the first max_slots items (w, s), then the other
+    // items one each (s = -1).
+    const int n_split_units = split ? p.split.max_slots * kMaxSeg : 0;
+    const int n_units = split ? n_split_units + p.items - p.split.max_slots : p.items;
     // Publish one record; SEL/POOL/CORR records are followed by their K/V tiles.
     auto emit = [&](const Rec& rec, const Chunk& ck, long long lrow) -> bool {
       const int ri = icount % kRecs;
@@ -350,18 +289,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
 
-    int w = 0, seg = 0, nseg = 0;
-    while (ok && next_unit(w, seg, nseg)) {
+    for (int u = next_work(); u < n_units && ok; u = next_work()) {
+      const bool vunit = u < n_split_units;
+      const int w = vunit ? u / kMaxSeg : u - n_split_units + p.split.max_slots;
+      const int seg = vunit ? u % kMaxSeg : -1;
       const Chunk ck = make_chunk(p, w);
       const long long lrow = ((long long)ck.h * a.Nt + ck.t) * a.Nb;
       const int nsel = clampi(a.sel_counts[(long long)ck.h * a.Nt + ck.t], 0, a.Nb);
       const int npr = a.corr ? clampi(a.pr_counts[(long long)ck.h * a.Nt + ck.t], 0, a.Nb) : 0;
-      // Q tile of the chunk.
-      {
+      // Q tile of the chunk (a split unit loads it once it knows it runs).
+      auto load_q = [&]() -> bool {
         const int qs = qcount & 1;
-        if (lane == 0) ok = mbar_wait(smem_u32(&q_empty[qs]), ((qcount >> 1) & 1) ^ 1, wc);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
+        bool good = true;
+        if (lane == 0) good = mbar_wait(smem_u32(&q_empty[qs]), ((qcount >> 1) & 1) ^ 1, wc);
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) return false;
         if (lane == 0) {
           const uint32_t qb = smem_u32(&q_full[qs]);
           mbar_arrive_expect_tx(qb, (uint32_t)C::kTileBytes);
@@ -371,6 +313,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ck.t * a.tile_q + ck.p0, ck.h * a.G + ck.g0);
         }
         ++qcount;
+        return true;
+      };
+      if (!vunit) {
+        ok = load_q();
+        if (!ok) break;
       }
       // Selected blocks up to the first one past the chunk (fpv2/kernel.py:249-255).
       int n_sel_items = 0, brk = nsel;
@@ -410,34 +357,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         n_corr_items = (npr + 63) / 64;   // 64 entries (high + low parts) per item
       }
       const int n_total = n_sel_items + n_corr_items;
-      // First visit of a long item with a slot: cut it into segments and queue
-      // segments 1.. for the other CTAs (this CTA runs segment 0).
-      if (split && nseg == 0 && w < p.split.max_slots && n_total > 2 * kSegLen) {
-        const int want = min(kMaxSeg, (n_total + kSegLen - 1) / kSegLen);
-        int pushed = 1;
-        if (lane == 0) {
-          const int base = atomicAdd(&p.split.hdr[1], want - 1);
-          if (base < 0 || base + want - 1 > p.split.qcap) {   // cannot happen: qcap covers every slot
-            atomicOr(wc.status, STATUS_BAD_SPLIT);
-            pushed = 0;
-          } else {
-            p.split.recs[w] = make_int4(w, want, 0, 0);
-            for (int s2 = 1; s2 < want; ++s2)
-              p.split.entries[base + s2 - 1] = make_int4(w, s2, want, 0);
-            __threadfence();
-            for (int s2 = 1; s2 < want; ++s2) atomicExch(&p.split.flags[base + s2 - 1], 1);
-          }
-        }
-        pushed = __shfl_sync(0xffffffffu, pushed, 0);
-        nseg = pushed ? want : 0;
-      }
       // This unit's share [lo, hi) of the item's KV item sequence.
       int lo = 0, hi = n_total, part = -1;
-      if (nseg > 0) {
-        const int per = (n_total + nseg - 1) / nseg;
-        lo = min(n_total, seg * per);
-        hi = seg == nseg - 1 ? n_total : min(n_total, lo + per);
-        part = w * kMaxSeg + seg;
+      if (vunit) {
+        const int nseg = n_total > 2 * kSegLen ? min(kMaxSeg, (n_total + kSegLen - 1) / kSegLen) : 1;
+        if (seg >= nseg) {   // a unit this item does not need
+          if (pool_tiles) __syncwarp();   // pmask reads done before the next unit clears it
+          continue;
+        }
+        if (nseg > 1) {
+          const int per = (n_total + nseg - 1) / nseg;
+          lo = min(n_total, seg * per);
+          hi = seg == nseg - 1 ? n_total : min(n_total, lo + per);
+          part = w * kMaxSeg + seg;
+          if (seg == 0 && lane == 0) p.split.recs[w] = make_int4(w, nseg, 0, 0);
+        }
+        ok = load_q();
+        if (!ok) break;
       }
       const int n_items = max(1, hi - lo);
       int emitted = 0, kvi = 0;   // kvi: index in the item's KV item sequence
@@ -1107,24 +1043,17 @@ namespace {
 
 // Byte layout of the split scratch inside the caller's workspace.
 struct SplitLayout {
-  int max_slots = 0, qcap = 0;
-  size_t flags = 0, entries = 0, recs = 0, parts = 0, clear = 0, total = 0;
+  int max_slots = 0;
+  size_t recs = 0, parts = 0, clear = 0, total = 0;
 };
 
 SplitLayout split_layout(int max_slots, int Dt) {
   auto up = [](size_t x, size_t al) { return (x + al - 1) / al * al; };
   SplitLayout s;
   s.max_slots = max_slots;
-  s.qcap = max_slots * (kMaxSeg - 1);
-  size_t off = 16;   // hdr: work counter, queue tail, queue head, (unused)
-  s.flags = off;
-  off = up(off + 4 * (size_t)s.qcap, 16);
-  s.entries = off;
-  off += 16 * (size_t)s.qcap;
-  s.recs = off;
-  off += 16 * (size_t)max_slots;
-  s.clear = off;     // everything before the partials is zeroed before each launch
-  s.parts = up(off, 256);
+  s.recs = 16;       // after the 16-byte work counter
+  s.clear = s.recs + 16 * (size_t)max_slots;   // zeroed before each launch
+  s.parts = up(s.clear, 256);
   s.total = s.parts + 4 * (size_t)max_slots * kMaxSeg * (128 * Dt + 256);
   return s;
 }
@@ -1174,19 +1103,15 @@ cudaError_t launch_attn_tc_impl(const AttnArgs& a, const TcLaunch& L, void* work
     if (slots > 0) {
       sl = split_layout(slots, split_tile_width(a));
       char* base = reinterpret_cast<char*>(workspace);
-      p.split.hdr = reinterpret_cast<int*>(base);
-      p.split.flags = reinterpret_cast<int*>(base + sl.flags);
-      p.split.entries = reinterpret_cast<int4*>(base + sl.entries);
       p.split.recs = reinterpret_cast<int4*>(base + sl.recs);
       p.split.partials = reinterpret_cast<float*>(base + sl.parts);
       p.split.max_slots = sl.max_slots;
-      p.split.qcap = sl.qcap;
     }
   }
 
   CUtensorMap m[6];
   if (!encode_attn_maps(a, m)) return cudaErrorInvalidValue;
-  const int grid = max(1, min(L.num_sms, p.items));
+  const int grid = max(1, min(L.num_sms, p.items + p.split.max_slots * (kMaxSeg - 1)));
   cudaError_t e = cudaSuccess;
   if (sched != nullptr) {
     e = cudaMemsetAsync(sched, 0, p.split.max_slots > 0 ? sl.clear : sizeof(int), stream);
