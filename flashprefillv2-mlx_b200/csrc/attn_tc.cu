@@ -319,21 +319,47 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = load_q();
         if (!ok) break;
       }
-      // Selected blocks up to the first one past the chunk (fpv2/kernel.py:249-255).
+      // A split unit first bounds the item's KV item count from its counts alone
+      // (every listed block once, every pooled tile or 64 gathered entries once)
+      // and skips at once when the item needs no segment s.
+      int nseg = 1;
+      if (vunit) {
+        const int ub = nsel * bk_sub +
+                       (a.corr ? (pool_tiles ? min(npr, (a.Nb + 127) / 128) : (npr + 63) / 64) : 0);
+        if (ub > 2 * kSegLen) nseg = min(kMaxSeg, (ub + kSegLen - 1) / kSegLen);
+        if (seg >= nseg) continue;   // a unit this item does not need
+      }
+      // Selected blocks up to the first one past the chunk (fpv2/kernel.py:249-255),
+      // four independent 32-entry loads in flight per step.
       int n_sel_items = 0, brk = nsel;
-      for (int i0 = 0; i0 < nsel; i0 += 32) {
-        const int i = i0 + lane;
-        const bool in = i < nsel;
-        const int blk = in ? clampi(a.sel_ids[lrow + i], 0, a.Nb - 1) : 0;
-        const long long bstart = (long long)blk * a.block_k;
-        const unsigned stop = __ballot_sync(0xffffffffu, in && bstart > ck.abs_last);
-        const int lim = stop ? (__ffs(stop) - 1) : 32;
-        int contrib = 0;
-        if (in && lane < lim) contrib = (int)min((long long)bk_sub, (ck.abs_last - bstart) / 128 + 1);
+      for (int i0 = 0; i0 < nsel; i0 += 128) {
+        int blk4[4];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) contrib += __shfl_xor_sync(0xffffffffu, contrib, o);
-        n_sel_items += contrib;
-        if (stop) { brk = i0 + lim; break; }
+        for (int x = 0; x < 4; ++x) {
+          const int i = i0 + 32 * x + lane;
+          blk4[x] = i < nsel ? clampi(a.sel_ids[lrow + i], 0, a.Nb - 1) : 0;
+        }
+        bool stopped = false;
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          const int c0 = i0 + 32 * x;
+          if (c0 >= nsel) break;
+          const bool in = c0 + lane < nsel;
+          const long long bstart = (long long)blk4[x] * a.block_k;
+          const unsigned stop = __ballot_sync(0xffffffffu, in && bstart > ck.abs_last);
+          const int lim = stop ? (__ffs(stop) - 1) : 32;
+          int contrib = 0;
+          if (in && lane < lim) contrib = (int)min((long long)bk_sub, (ck.abs_last - bstart) / 128 + 1);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) contrib += __shfl_xor_sync(0xffffffffu, contrib, o);
+          n_sel_items += contrib;
+          if (stop) {
+            brk = c0 + lim;
+            stopped = true;
+            break;
+          }
+        }
+        if (stopped) break;
       }
       // Pooled correction items.
       int n_corr_items = 0;
@@ -358,13 +384,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int n_total = n_sel_items + n_corr_items;
       // This unit's share [lo, hi) of the item's KV item sequence.
+      // (segments are equal shares of the exact count; the bound only sets nseg)
       int lo = 0, hi = n_total, part = -1;
       if (vunit) {
-        const int nseg = n_total > 2 * kSegLen ? min(kMaxSeg, (n_total + kSegLen - 1) / kSegLen) : 1;
-        if (seg >= nseg) {   // a unit this item does not need
-          if (pool_tiles) __syncwarp();   // pmask reads done before the next unit clears it
-          continue;
-        }
         if (nseg > 1) {
           const int per = (n_total + nseg - 1) / nseg;
           lo = min(n_total, seg * per);
@@ -377,6 +399,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int n_items = max(1, hi - lo);
       int emitted = 0, kvi = 0;   // kvi: index in the item's KV item sequence
+      // With one 128-key item per listed block, the items before the first block
+      // past the chunk are the blocks themselves: start at lo's 32-entry chunk.
+      const int sel_start = bk_sub == 1 ? min(lo, brk) / 32 * 32 : 0;
+      kvi = sel_start;
       auto make_rec = [&](int kind, int kstart, int nvalid) {
         Rec r;
         r.kind = kind;
@@ -389,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++emitted;
         return r;
       };
-      for (int i0 = 0; i0 < brk && ok && kvi < hi; i0 += 32) {
+      for (int i0 = sel_start; i0 < brk && ok && kvi < hi; i0 += 32) {
         const int i = i0 + lane;
         const int blk = i < brk ? clampi(a.sel_ids[lrow + i], 0, a.Nb - 1) : 0;
         const int cnt = min(32, brk - i0);
@@ -916,62 +942,70 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Merge the segments of every split work item: per row,
 //   out = sum_s 2^(m_s - m) O_s / sum_s 2^(m_s - m) l_s,  m = max_s m_s,
-// the same combination the epilogue applies to the two key halves. One CTA per
-// slot (grid-stride), one thread per 8 output columns (one 16-byte store) of a row.
+// the same combination the epilogue applies to the two key halves. Grid
+// (slot, group of 8 rows); one thread per 8 output columns (one 16-byte store)
+// of a row, with the segments' loads unrolled so that they overlap.
 template <int D, int DT>
-__global__ void __launch_bounds__(512) attn_combine_kernel(Params p) {
+__global__ void __launch_bounds__(8 * (D / 8)) attn_combine_kernel(Params p) {
   const AttnArgs& a = p.a;
   constexpr int kPart = 128 * D + 256;
   constexpr int kGroups = D / 8;
-  for (int slot = blockIdx.x; slot < p.split.max_slots; slot += gridDim.x) {
-    const int4 rec = p.split.recs[slot];
-    const int nseg = min(rec.y, kMaxSeg);
-    if (nseg <= 0) continue;
-    if (rec.x != slot || rec.x >= p.items) {   // bounds check failed: report, skip the slot
-      if (threadIdx.x == 0) atomicOr(p.status, STATUS_BAD_SPLIT);
-      continue;
-    }
-    const Chunk ck = make_chunk(p, rec.x);
-    const float* base = p.split.partials + (size_t)slot * kMaxSeg * kPart;
-    for (int idx = threadIdx.x; idx < 128 * kGroups; idx += blockDim.x) {
-      const int r = idx / kGroups, c0 = (idx % kGroups) * 8;
-      float m = kFiniteMin;
-      for (int sg = 0; sg < nseg; ++sg) m = fmaxf(m, base[(size_t)sg * kPart + 128 * D + r]);
-      float den = 0.f, acc[8];
+  const int slot = blockIdx.x;
+  const int4 rec = p.split.recs[slot];
+  const int nseg = min(rec.y, kMaxSeg);
+  if (nseg <= 0) return;
+  if (rec.x != slot || rec.x >= p.items) {   // bounds check failed: report, skip the slot
+    if (threadIdx.x == 0 && blockIdx.y == 0) atomicOr(p.status, STATUS_BAD_SPLIT);
+    return;
+  }
+  const Chunk ck = make_chunk(p, rec.x);
+  const float* base = p.split.partials + (size_t)slot * kMaxSeg * kPart;
+  const int r = blockIdx.y * 8 + threadIdx.x / kGroups;
+  const int c0 = (threadIdx.x % kGroups) * 8;
+  float ms[kMaxSeg], ls[kMaxSeg];
+  float m = kFiniteMin;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-      for (int sg = 0; sg < nseg; ++sg) {
-        const float* ps = base + (size_t)sg * kPart;
-        const float wgt = ex2(ps[128 * D + r] - m);
-        den = fmaf(wgt, ps[128 * D + 128 + r], den);
-        const float4 u0 = *reinterpret_cast<const float4*>(ps + r * D + c0);
-        const float4 u1 = *reinterpret_cast<const float4*>(ps + r * D + c0 + 4);
-        acc[0] = fmaf(wgt, u0.x, acc[0]);
-        acc[1] = fmaf(wgt, u0.y, acc[1]);
-        acc[2] = fmaf(wgt, u0.z, acc[2]);
-        acc[3] = fmaf(wgt, u0.w, acc[3]);
-        acc[4] = fmaf(wgt, u1.x, acc[4]);
-        acc[5] = fmaf(wgt, u1.y, acc[5]);
-        acc[6] = fmaf(wgt, u1.z, acc[6]);
-        acc[7] = fmaf(wgt, u1.w, acc[7]);
-      }
-      const float inv = den > 0.f ? 1.f / den : 0.f;
-      const uint4 v = make_uint4(pack2<DT>(acc[0] * inv, acc[1] * inv), pack2<DT>(acc[2] * inv, acc[3] * inv),
-                                 pack2<DT>(acc[4] * inv, acc[5] * inv), pack2<DT>(acc[6] * inv, acc[7] * inv));
-      const int P = ck.c * 128 + r;
-      const long long head = (long long)ck.h * a.G + P / a.tile_q;
-      const long long pos = (long long)ck.t * a.tile_q + P % a.tile_q;
-      if (c0 >= a.D) continue;   // head_dim 96 runs on the 128-wide tiles
-      if (a.out_mc != nullptr) {
-        multimem_st16(reinterpret_cast<char*>(a.out_mc) +
-                          (((head + a.mc_head_offset) * a.Lq_pad + pos) * a.D + c0) * 2, v);
-      } else {
-        *reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.out) +
-                                  ((head * a.Lq_pad + pos) * a.D + c0) * 2) = v;
-      }
+  for (int sg = 0; sg < kMaxSeg; ++sg) {
+    ms[sg] = sg < nseg ? base[(size_t)sg * kPart + 128 * D + r] : kFiniteMin;
+    ls[sg] = sg < nseg ? base[(size_t)sg * kPart + 128 * D + 128 + r] : 0.f;
+    m = fmaxf(m, ms[sg]);
+  }
+  float den = 0.f, acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+  for (int sg = 0; sg < kMaxSeg; ++sg) {
+    if (sg < nseg) {
+      const float* ps = base + (size_t)sg * kPart + r * D + c0;
+      const float wgt = ex2(ms[sg] - m);
+      den = fmaf(wgt, ls[sg], den);
+      const float4 u0 = *reinterpret_cast<const float4*>(ps);
+      const float4 u1 = *reinterpret_cast<const float4*>(ps + 4);
+      acc[0] = fmaf(wgt, u0.x, acc[0]);
+      acc[1] = fmaf(wgt, u0.y, acc[1]);
+      acc[2] = fmaf(wgt, u0.z, acc[2]);
+      acc[3] = fmaf(wgt, u0.w, acc[3]);
+      acc[4] = fmaf(wgt, u1.x, acc[4]);
+      acc[5] = fmaf(wgt, u1.y, acc[5]);
+      acc[6] = fmaf(wgt, u1.z, acc[6]);
+      acc[7] = fmaf(wgt, u1.w, acc[7]);
     }
   }
-  if (a.out_mc != nullptr) asm volatile("fence.acq_rel.sys;" ::: "memory");
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  const uint4 v = make_uint4(pack2<DT>(acc[0] * inv, acc[1] * inv), pack2<DT>(acc[2] * inv, acc[3] * inv),
+                             pack2<DT>(acc[4] * inv, acc[5] * inv), pack2<DT>(acc[6] * inv, acc[7] * inv));
+  const int P = ck.c * 128 + r;
+  const long long head = (long long)ck.h * a.G + P / a.tile_q;
+  const long long pos = (long long)ck.t * a.tile_q + P % a.tile_q;
+  if (c0 < a.D) {   // head_dim 96 runs on the 128-wide tiles
+    if (a.out_mc != nullptr) {
+      multimem_st16(reinterpret_cast<char*>(a.out_mc) +
+                        (((head + a.mc_head_offset) * a.Lq_pad + pos) * a.D + c0) * 2, v);
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+    } else {
+      *reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.out) + ((head * a.Lq_pad + pos) * a.D + c0) * 2) = v;
+    }
+  }
 }
 
 template <int D>
@@ -1094,9 +1128,11 @@ cudaError_t launch_attn_tc_impl(const AttnArgs& a, const TcLaunch& L, void* work
   p.split = Split{};
   if (p.items == 0) return cudaSuccess;
 
-  // KV-segment split when the workspace holds the scratch for some slots.
+  // KV-segment split when the work items are few per SM (so that one long item
+  // outlasts an SM's share of the rest) and the workspace holds the scratch.
   SplitLayout sl;
-  if (sched != nullptr && reinterpret_cast<uintptr_t>(workspace) % 256 == 0) {
+  const bool few_items = p.items < 32 * L.num_sms;
+  if (few_items && sched != nullptr && reinterpret_cast<uintptr_t>(workspace) % 256 == 0) {
     int slots = std::min(p.items, 4 * a.Hkv * p.nch);
     while (slots > 0 && split_layout(slots, split_tile_width(a)).total > (size_t)workspace_bytes)
       slots /= 2;
@@ -1117,7 +1153,7 @@ cudaError_t launch_attn_tc_impl(const AttnArgs& a, const TcLaunch& L, void* work
     e = cudaMemsetAsync(sched, 0, p.split.max_slots > 0 ? sl.clear : sizeof(int), stream);
     if (e != cudaSuccess) return e;
   }
-  const int cgrid = std::max(1, std::min(p.split.max_slots, L.num_sms));
+  const dim3 cgrid(std::max(1, p.split.max_slots), 16);
   const bool gather = a.corr && a.pooled_dt != a.dt;   // float32 pooled K/V
 #define FPV2_ATTN_LAUNCH(DD, TT, VV, GG)                                                    \
   {                                                                                         \
@@ -1126,7 +1162,7 @@ cudaError_t launch_attn_tc_impl(const AttnArgs& a, const TcLaunch& L, void* work
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
     if (e != cudaSuccess) return e;                                                         \
     attn_tc_kernel<DD, TT, VV, GG><<<grid, kThreads, smem, stream>>>(m[0], m[1], m[2], m[3], m[4], m[5], p); \
-    if (p.split.max_slots > 0) attn_combine_kernel<DD, TT><<<cgrid, 512, 0, stream>>>(p);    \
+    if (p.split.max_slots > 0) attn_combine_kernel<DD, TT><<<cgrid, DD, 0, stream>>>(p);     \
   }
 #define FPV2_ATTN_TYPES(DD)                                                                 \
   {                                                                                         \
