@@ -176,15 +176,31 @@ static int check_select_geom(const SelectGeom& g) {
   return FPV2_OK;
 }
 
-// Selection with lists and/or mask: tcgen05 kernel when the shape fits.
+// Selection with lists and/or mask: tcgen05 kernel when the shape fits. float32
+// pooled keys with 16-bit queries run on it too when the workspace holds their
+// three 16-bit parts; otherwise (and for float32 queries) on the CUDA cores.
 static int run_select(const SelectGeom& g, const void* q, int q_dt, const void* pk, int pk_dt,
                       uint8_t* mask, const SelectLists& lists, const DeviceInfo& d,
-                      cudaStream_t stream) {
+                      void* workspace, int64_t workspace_bytes, cudaStream_t stream) {
   cudaError_t e;
   const bool aligned = (reinterpret_cast<uintptr_t>(q) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(pk) % 16 == 0);
+  int nparts = 1;
+  const int* k_exp = nullptr;
+  if (pk_dt == DT_F32 && q_dt != DT_F32 && aligned && select_tc_supported(g, q_dt) &&
+      workspace != nullptr && reinterpret_cast<uintptr_t>(workspace) % 256 == 0 &&
+      workspace_bytes >= (int64_t)pk_split3_bytes(g.Hkv, g.Nb, g.D)) {
+    e = launch_pk_split3(reinterpret_cast<const float*>(pk), workspace, q_dt, g.Hkv, g.Nb, g.D,
+                         &k_exp, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "pooled-key split launch");
+    pk = workspace;
+    pk_dt = q_dt;
+    nparts = 3;
+  }
   if (q_dt == pk_dt && aligned && select_tc_supported(g, q_dt)) {
     SelectTcArgs a;
+    a.nparts = nparts;
+    a.k_exp = k_exp;
     a.g = g;
     const int R = g.G * g.tile_q;
     a.NC = R < 128 ? R : 128;
@@ -286,7 +302,7 @@ int fpv2_block_select(const void* q, int q_dtype, const void* pooled_k, int k_dt
                       int32_t query_length, float scale, int32_t block_k, int32_t tile_q,
                       float alpha, int32_t sink_tokens, int32_t window_tokens,
                       int32_t last_n_blocks, uint8_t* selected, float* raw_scores,
-                      void* stream) {
+                      void* workspace, int64_t workspace_bytes, void* stream) {
   if (!valid_dtype(q_dtype) || !valid_dtype(k_dtype))
     return fail(FPV2_ERR_INVALID_ARGUMENT, "unknown dtype code");
   SelectGeom g;
@@ -316,7 +332,7 @@ int fpv2_block_select(const void* q, int q_dtype, const void* pooled_k, int k_dt
   if (rc != FPV2_OK) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   SelectLists none{nullptr, nullptr, nullptr, nullptr};
-  rc = run_select(g, q, q_dtype, pooled_k, k_dtype, selected, none, *d, s);
+  rc = run_select(g, q, q_dtype, pooled_k, k_dtype, selected, none, *d, workspace, workspace_bytes, s);
   if (rc != FPV2_OK) return rc;
   if (raw_scores != nullptr) {
     cudaError_t e = launch_raw_scores(g, q, q_dtype, pooled_k, k_dtype, raw_scores, s);
@@ -361,7 +377,7 @@ int fpv2_index_stage(const void* q, const void* k, const void* v, int dtype,
                      int32_t window_tokens, int32_t last_n_blocks, int pooled_dtype,
                      void* pooled_k, void* pooled_v, int32_t* selected_ids,
                      int32_t* selected_counts, int32_t* pruned_ids, int32_t* pruned_counts,
-                     uint8_t* selected, void* stream) {
+                     uint8_t* selected, void* workspace, int64_t workspace_bytes, void* stream) {
   if (dtype != DT_F16 && dtype != DT_BF16 && dtype != DT_F32)
     return fail(FPV2_ERR_INVALID_ARGUMENT, "unknown dtype code");
   if (pooled_dtype != dtype && pooled_dtype != DT_F32)
@@ -411,7 +427,16 @@ int fpv2_index_stage(const void* q, const void* k, const void* v, int dtype,
   cudaError_t e = launch_pool(pa, 2, dtype, pooled_dtype, s);
   if (e != cudaSuccess) return cuda_fail(e, "pool launch");
   SelectLists lists{selected_ids, selected_counts, pruned_ids, pruned_counts};
-  return run_select(g, q, dtype, pooled_k, pooled_dtype, selected, lists, *d, s);
+  return run_select(g, q, dtype, pooled_k, pooled_dtype, selected, lists, *d, workspace,
+                    workspace_bytes, s);
+}
+
+int64_t fpv2_select_workspace_bytes(int q_dtype, int k_dtype, int32_t kv_heads,
+                                    int32_t num_blocks, int32_t head_dim) {
+  if (k_dtype != DT_F32 || (q_dtype != DT_BF16 && q_dtype != DT_F16) || kv_heads <= 0 ||
+      num_blocks <= 0 || head_dim <= 0)
+    return 0;
+  return (int64_t)pk_split3_bytes(kv_heads, num_blocks, head_dim);
 }
 
 namespace fpv2 {

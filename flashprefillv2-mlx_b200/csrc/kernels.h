@@ -136,8 +136,16 @@ struct SelectTcArgs {
   int32_t* sel_counts;
   int32_t* pr_ids;
   int32_t* pr_counts;
+  int nparts = 1;       // 16-bit parts of the pooled keys ([nparts][Hkv][Nb][D]; 3: float32 keys)
+  const int* k_exp = nullptr;   // nparts == 3: per-KV-head exponent of the parts
 };
 bool select_tc_supported(const SelectGeom& g, int dt);
+// float32 pooled keys [Hkv][Nb][D] -> three 16-bit parts [3][Hkv][Nb][D] of dtype
+// dt, each head scaled by 2^-k_exp[h] into the type's range (select_tc.cu).
+// `out` (256-byte aligned) holds pk_split3_bytes(Hkv, Nb, D); *k_exp points into it.
+size_t pk_split3_bytes(int Hkv, int Nb, int D);
+cudaError_t launch_pk_split3(const float* pk, void* out, int dt, int Hkv, int Nb, int D,
+                             const int** k_exp, cudaStream_t stream);
 cudaError_t launch_select_tc(const SelectTcArgs& a, const void* q, const void* pk,
                              const TcLaunch& L, cudaStream_t stream);
 

@@ -26,6 +26,8 @@
 //           exponentials and each SM sub-partition has two warps issuing ex2.
 // Work items are (kv head, tile) with tiles latest-first; CTA c keeps KV head
 // c % Hkv whenever the grid is a multiple of Hkv.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -54,6 +56,8 @@ struct Params {
   SelectGeom g;
   int NC, box_rows, n_chunks;
   int k_stages;                      // pooled-K ring slots in use (<= kKStagesMax)
+  int nparts;                        // 16-bit parts of the pooled keys (3: float32 pooled K)
+  const int* k_exp;                  // nparts == 3: per-KV-head exponent of the parts, else null
   uint32_t idesc;
   float scale_log2;
   uint8_t* mask;
@@ -218,12 +222,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int hh = 0; hh < C::kHalves; ++hh)
               tma_load_3d(q_smem + qs * C::kQBytes + hh * p.NC * 128, &tmap_q, qb, hh * 64,
                           it.t * g.tile_q + p0, it.h * g.G + g0);
-            for (int m = 0; m < it.n_mt; ++m) {
-              const int s = m % KS;
+            for (int mi = 0; mi < it.n_mt * p.nparts; ++mi) {   // (tile, part) pairs
+              const int m = mi / p.nparts, part = mi % p.nparts;
+              const int s = mi % KS;
               ok = mbar_wait(smem_u32(&k_empty[s]), (kuse[s] & 1) ^ 1, wc);
               if (!ok) break;
               ++kuse[s];
-              const int tag = it.h * 4096 + m;
+              const int tag = (it.h * 4096 + m) * 4 + part;
               const uint32_t kb = smem_u32(&k_full[s]);
               if (ktag[s] == tag) {
                 mbar_arrive(kb);   // tile still resident
@@ -233,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   #pragma unroll
                 for (int hh = 0; hh < C::kHalves; ++hh)
                   tma_load_3d(k_smem + s * C::kKBytes + hh * 128 * 128, &tmap_k, kb, hh * 64, m * 128,
-                              it.h);
+                              part * g.Hkv + it.h);
               }
             }
           }
@@ -270,15 +275,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tma_load_3d(q_smem + qs * C::kQBytes + hh * p.NC * 128, &tmap_q, qb, hh * 64,
                             it.t * g.tile_q + p0, it.h * g.G + g0);
             }
-            for (int m = 0; m < nmax && ok; ++m) {
+            for (int mi = 0; mi < nmax * p.nparts && ok; ++mi) {   // (tile, part) pairs
+              const int m = mi / p.nparts, part = mi % p.nparts;
   #pragma unroll
               for (int x = 0; x < 2; ++x) {
                 if (m >= nmt[x] || !ok) continue;
-                const int s = m % KS;
+                const int s = mi % KS;
                 ok = mbar_wait(smem_u32(&k_empty[s]), (kuse[s] & 1) ^ 1, wc);
                 if (!ok) break;
                 ++kuse[s];
-                const int tag = its[x].h * 4096 + m;
+                const int tag = (its[x].h * 4096 + m) * 4 + part;
                 const uint32_t kb = smem_u32(&k_full[s]);
                 if (ktag[s] == tag) {
                   mbar_arrive(kb);   // tile still resident
@@ -288,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   #pragma unroll
                   for (int hh = 0; hh < C::kHalves; ++hh)
                     tma_load_3d(k_smem + s * C::kKBytes + hh * 128 * 128, &tmap_k, kb, hh * 64, m * 128,
-                                its[x].h);
+                                part * g.Hkv + its[x].h);
                 }
               }
             }
@@ -324,29 +330,35 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = mbar_wait(smem_u32(&q_full[qs]), (qcount / C::kQStages) & 1, wc);
             if (!ok) break;
             ++qcount;
-            for (int m = 0; m < it.n_mt; ++m) {
-              const int s = m % KS;
-              ok = mbar_wait(smem_u32(&k_full[s]), kuse[s] & 1, wc);
-              if (!ok) break;
-              ++kuse[s];
-              const int tc = tcount[grp];
-              const int ts = grp * kSlotsPerGroup + tc % kSlotsPerGroup;
-              ok = mbar_wait(smem_u32(&t_empty[ts]), ((tc / kSlotsPerGroup) & 1) ^ 1, wc);
-              if (!ok) break;
-              ++tcount[grp];
-              tc_fence_after();
-              const uint32_t d_tmem = tmem_base + ts * 128;
+            for (int m = 0; m < it.n_mt && ok; ++m) {
+              int ts = 0;
+              // one score tile per m: the parts of the pooled keys accumulate into it
+              for (int part = 0; part < p.nparts && ok; ++part) {
+                const int s = (m * p.nparts + part) % KS;
+                ok = mbar_wait(smem_u32(&k_full[s]), kuse[s] & 1, wc);
+                if (!ok) break;
+                ++kuse[s];
+                if (part == 0) {
+                  const int tc = tcount[grp];
+                  ts = grp * kSlotsPerGroup + tc % kSlotsPerGroup;
+                  ok = mbar_wait(smem_u32(&t_empty[ts]), ((tc / kSlotsPerGroup) & 1) ^ 1, wc);
+                  if (!ok) break;
+                  ++tcount[grp];
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + ts * 128;
   #pragma unroll
-              for (int kk = 0; kk < D / 16; ++kk) {
-                const int hh = kk / 4, sub = kk % 4;
-                const uint64_t a_desc =
-                    sw128_desc(k_smem + s * C::kKBytes + hh * 128 * 128 + sub * 32, 16, 1024);
-                const uint64_t b_desc =
-                    sw128_desc(q_smem + qs * C::kQBytes + hh * p.NC * 128 + sub * 32, 16, 1024);
-                umma_ss(d_tmem, a_desc, b_desc, p.idesc, kk > 0 ? 1u : 0u);
+                for (int kk = 0; kk < D / 16; ++kk) {
+                  const int hh = kk / 4, sub = kk % 4;
+                  const uint64_t a_desc =
+                      sw128_desc(k_smem + s * C::kKBytes + hh * 128 * 128 + sub * 32, 16, 1024);
+                  const uint64_t b_desc =
+                      sw128_desc(q_smem + qs * C::kQBytes + hh * p.NC * 128 + sub * 32, 16, 1024);
+                  umma_ss(d_tmem, a_desc, b_desc, p.idesc, (part > 0 || kk > 0) ? 1u : 0u);
+                }
+                if (part == p.nparts - 1) umma_commit(smem_u32(&t_full[ts]));
+                umma_commit(smem_u32(&k_empty[s]));
               }
-              umma_commit(smem_u32(&t_full[ts]));
-              umma_commit(smem_u32(&k_empty[s]));
             }
             if (ok) umma_commit(smem_u32(&q_empty[qs]));
           }
@@ -370,22 +382,28 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = mbar_wait(smem_u32(&q_full[qsx[x]]), (qcount / C::kQStages) & 1, wc);
               ++qcount;
             }
-            for (int m = 0; m < nmax && ok; ++m) {
+            // (tile, part) pairs in the producer's order; the parts of one tile
+            // accumulate into one score tile of each item
+            int tsx[2] = {0, 0};
+            for (int mi = 0; mi < nmax * p.nparts && ok; ++mi) {
+              const int m = mi / p.nparts, part = mi % p.nparts;
   #pragma unroll
               for (int x = 0; x < 2; ++x) {
                 if (m >= nmt[x] || !ok) continue;
                 const int grp = (j + x) % kGroups;
-                const int s = m % KS;
+                const int s = mi % KS;
                 ok = mbar_wait(smem_u32(&k_full[s]), kuse[s] & 1, wc);
                 if (!ok) break;
                 ++kuse[s];
-                const int tc = tcount[grp];
-                const int ts = grp * kSlotsPerGroup + tc % kSlotsPerGroup;
-                ok = mbar_wait(smem_u32(&t_empty[ts]), ((tc / kSlotsPerGroup) & 1) ^ 1, wc);
-                if (!ok) break;
-                ++tcount[grp];
+                if (part == 0) {
+                  const int tc = tcount[grp];
+                  tsx[x] = grp * kSlotsPerGroup + tc % kSlotsPerGroup;
+                  ok = mbar_wait(smem_u32(&t_empty[tsx[x]]), ((tc / kSlotsPerGroup) & 1) ^ 1, wc);
+                  if (!ok) break;
+                  ++tcount[grp];
+                }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + ts * 128;
+                const uint32_t d_tmem = tmem_base + tsx[x] * 128;
                 const uint32_t qsm = q_smem + qsx[x] * C::kQBytes;
   #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
@@ -393,12 +411,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const uint64_t a_desc =
                       sw128_desc(k_smem + s * C::kKBytes + hh * 128 * 128 + sub * 32, 16, 1024);
                   const uint64_t b_desc = sw128_desc(qsm + hh * p.NC * 128 + sub * 32, 16, 1024);
-                  umma_ss(d_tmem, a_desc, b_desc, p.idesc, kk > 0 ? 1u : 0u);
+                  umma_ss(d_tmem, a_desc, b_desc, p.idesc, (part > 0 || kk > 0) ? 1u : 0u);
                 }
-                umma_commit(smem_u32(&t_full[ts]));
+                if (part == p.nparts - 1) umma_commit(smem_u32(&t_full[tsx[x]]));
                 umma_commit(smem_u32(&k_empty[s]));
                 // this item's query chunk is read for the last time
-                if (m == nmt[x] - 1) umma_commit(smem_u32(&q_empty[qsx[x]]));
+                if (m == nmt[x] - 1 && part == p.nparts - 1) umma_commit(smem_u32(&q_empty[qsx[x]]));
               }
             }
           }
@@ -421,7 +439,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ew = et >> 5;                    // 0..3 index among the group's warps
     const int bar_id = 1 + grp;                // the group's named barrier
     const unsigned lt = (1u << lane) - 1u;
-    const float c = p.scale_log2;              // > 0 on this path
     float2* stats = stats_all + grp * Nb;
     uint32_t* selw = words_all + grp * 4 * nwords;
     uint32_t* prw = selw + nwords;
@@ -438,6 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     named_bar_sync(bar_id, 128);
     for (int w = blockIdx.x + grp * gridDim.x; w < total_work; w += kGroups * gridDim.x) {
       const Item it = make_item(p, w);
+      // > 0 on this path; float32 pooled keys of a head scaled by 2^-e score at 2^e
+      const float c = p.k_exp == nullptr ? p.scale_log2 : ldexpf(p.scale_log2, p.k_exp[it.h]);
       const long long row_base = ((long long)it.h * g.Nt + it.t) * Nb;
       for (int cc = 0; cc < p.n_chunks; ++cc) {
         for (int m = 0; m < it.n_mt; ++m) {
@@ -711,12 +730,16 @@ cudaError_t launch_select_tc(const SelectTcArgs& a, const void* q, const void* p
   p.pr_counts = a.pr_counts;
   p.status = L.status;
   p.budget = L.budget;
+  p.nparts = a.nparts;
+  p.k_exp = a.k_exp;
 
   CUtensorMap tq, tk;
   if (!encode_tmap_3d(&tq, q, a.dt, (uint64_t)g.D, (uint64_t)g.Lq_pad, (uint64_t)g.Hq, 64,
                       (uint32_t)a.box_rows, (uint32_t)a.box_heads))
     return cudaErrorInvalidValue;
-  if (!encode_tmap_3d(&tk, pk, a.dt, (uint64_t)g.D, (uint64_t)g.Nb, (uint64_t)g.Hkv, 64, 128, 1))
+  // (pooled keys [nparts][Hkv][Nb][D]: part p of head h is "head" p * Hkv + h)
+  if (!encode_tmap_3d(&tk, pk, a.dt, (uint64_t)g.D, (uint64_t)g.Nb, (uint64_t)g.Hkv * a.nparts, 64,
+                      128, 1))
     return cudaErrorInvalidValue;
 
   const int total = g.Hkv * g.Nt;
@@ -743,6 +766,94 @@ cudaError_t launch_select_tc(const SelectTcArgs& a, const void* q, const void* p
   else if (g.D == 256) FPV2_SELECT_LAUNCH(256)
   else FPV2_SELECT_LAUNCH(128)
 #undef FPV2_SELECT_LAUNCH
+  return cudaGetLastError();
+}
+
+namespace {
+
+constexpr size_t up_to(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// float32 pooled keys -> three 16-bit parts, out[p][i] for p = 0, 1, 2:
+// round(y), round(y - part0), round(y - part0 - part1) with y = x * 2^-e[h].
+// Their sum carries about 24 (bf16) or 33 (fp16) significant bits, so Q.K^T
+// accumulated over the parts in fp32 equals the float32 product to within
+// float32 rounding (fp16 parts of magnitudes below 2^-14 keep an absolute
+// precision of 2^-25). e[h] >= 0 is the smallest exponent that brings KV head
+// h's largest magnitude within the 16-bit type's range: 0 for any pooled keys
+// of 16-bit inputs, and 0 for non-finite maxima (which score as in float32);
+// the selection kernel scores head h at scale * 2^e[h].
+//
+// pk_absmax_kernel: grid (blocks, Hkv), the heads' maximum magnitudes as
+// order-preserving bit patterns (non-negative floats order as integers).
+__global__ void __launch_bounds__(256) pk_absmax_kernel(const float* __restrict__ pk,
+                                                        unsigned* amax, long long per_head) {
+  const int h = blockIdx.y;
+  const float* src = pk + (long long)h * per_head;
+  float m = 0.f;
+  for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < per_head;
+       i += (long long)gridDim.x * 256)
+    m = fmaxf(m, fabsf(src[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0 && m > 0.f) atomicMax(&amax[h], __float_as_uint(m));
+}
+
+// Smallest e >= 0 with amax * 2^-e <= limit (0 for non-finite or in-range maxima).
+__device__ __forceinline__ int range_exponent(float amax, float limit) {
+  if (!(amax > limit) || !(amax <= 3.402823466e38f)) return 0;
+  int e = ilogbf(amax) - ilogbf(limit);
+  if (ldexpf(amax, -e) > limit) ++e;
+  return e;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(256) pk_split3_kernel(const float* __restrict__ pk, void* out,
+                                                        const unsigned* __restrict__ amax,
+                                                        int* k_exp, int Hkv, long long per_head) {
+  using T = typename Elem<DT>::T;
+  // largest finite magnitude of the part type
+  const float limit = DT == DT_F16 ? 65504.f : 3.38953139e38f;
+  T* o = reinterpret_cast<T*>(out);
+  const long long n = (long long)Hkv * per_head;
+  if (blockIdx.x == 0)
+    for (int h = threadIdx.x; h < Hkv; h += 256) k_exp[h] = range_exponent(__uint_as_float(amax[h]), limit);
+  for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < n; i += (long long)gridDim.x * 256) {
+    const int e = range_exponent(__uint_as_float(amax[i / per_head]), limit);
+    const float x = e ? ldexpf(pk[i], -e) : pk[i];
+    const T h = Elem<DT>::from_f(x);
+    const float r1 = x - Elem<DT>::to_f(h);
+    const T m = Elem<DT>::from_f(r1);
+    const float r2 = r1 - Elem<DT>::to_f(m);
+    o[i] = h;
+    o[n + i] = m;
+    o[2 * n + i] = Elem<DT>::from_f(r2);
+  }
+}
+
+}  // namespace
+
+size_t pk_split3_bytes(int Hkv, int Nb, int D) {
+  return up_to((size_t)3 * Hkv * Nb * D * 2, 256) + 2 * sizeof(int) * (size_t)Hkv;
+}
+
+cudaError_t launch_pk_split3(const float* pk, void* out, int dt, int Hkv, int Nb, int D,
+                             const int** k_exp, cudaStream_t stream) {
+  const long long per_head = (long long)Nb * D;
+  const long long n = per_head * Hkv;
+  unsigned* amax = reinterpret_cast<unsigned*>(static_cast<char*>(out) + up_to((size_t)3 * n * 2, 256));
+  int* ex = reinterpret_cast<int*>(amax + Hkv);
+  *k_exp = ex;
+  cudaError_t e = cudaMemsetAsync(amax, 0, sizeof(unsigned) * Hkv, stream);
+  if (e != cudaSuccess) return e;
+  const int gx = (int)std::max<long long>(1, std::min<long long>((per_head + 255) / 256, 64));
+  pk_absmax_kernel<<<dim3(gx, Hkv), 256, 0, stream>>>(pk, amax, per_head);
+  const int grid = (int)std::max<long long>(1, std::min<long long>((n + 255) / 256, 4096));
+  if (dt == DT_BF16)
+    pk_split3_kernel<DT_BF16><<<grid, 256, 0, stream>>>(pk, out, amax, ex, Hkv, per_head);
+  else if (dt == DT_F16)
+    pk_split3_kernel<DT_F16><<<grid, 256, 0, stream>>>(pk, out, amax, ex, Hkv, per_head);
+  else
+    return cudaErrorInvalidValue;
   return cudaGetLastError();
 }
 

@@ -42,7 +42,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
          ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
          ctypes.c_int32, ctypes.c_float, ctypes.c_int32, ctypes.c_int32, ctypes.c_float,
          ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
-         ctypes.c_void_p],
+         ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p],
+    ),
+    "fpv2_select_workspace_bytes": (
+        ctypes.c_int64,
+        [ctypes.c_int, ctypes.c_int, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32],
     ),
     "fpv2_compact_block_indices": (
         ctypes.c_int,
@@ -57,7 +61,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
          ctypes.c_int32, ctypes.c_int32, ctypes.c_float, ctypes.c_int32, ctypes.c_int32,
          ctypes.c_float, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int,
          ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p],
+         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p],
     ),
     "fpv2_sparse_attention": (
         ctypes.c_int,
@@ -204,6 +208,21 @@ def attention_workspace(q: torch.Tensor, kv_heads: int, padded_k_len: int, block
         tile_q, dtype_code(pooled_dtype), 1 if mean_correction else 0)
     return torch.empty((max(int(nbytes), ATTN_WORKSPACE_BYTES) + 3) // 4, dtype=torch.int32,
                        device=q.device)
+
+
+def select_workspace(q: torch.Tensor, pooled_dtype: torch.dtype, kv_heads: int, num_blocks: int,
+                     head_dim: int) -> torch.Tensor | None:
+    """Device workspace that lets the selection score float32 pooled keys on the
+    tensor cores (``fpv2_select_workspace_bytes``); None when none is needed."""
+    nbytes = int(lib().fpv2_select_workspace_bytes(
+        dtype_code(q.dtype), dtype_code(pooled_dtype), kv_heads, num_blocks, head_dim))
+    if nbytes <= 0:
+        return None
+    return torch.empty((nbytes + 3) // 4, dtype=torch.int32, device=q.device)
+
+
+def workspace_args(ws: torch.Tensor | None) -> tuple[int | None, int]:
+    return (None, 0) if ws is None else (ws.data_ptr(), ws.numel() * 4)
 
 
 def set_wait_budget_ms(milliseconds: float) -> None:

@@ -278,13 +278,14 @@ def index_stage(
     mask = (torch.empty((kv_heads, num_tiles, num_blocks), dtype=torch.uint8, device=dev)
             if return_mask else None)
     qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
+    ws = _lib.select_workspace(qc, pdt, kv_heads, num_blocks, head_dim)
     _lib.check(_lib.lib().fpv2_index_stage(
         _lib.ptr(qc), _lib.ptr(kc), _lib.ptr(vc), _lib.dtype_code(q.dtype), query_heads,
         kv_heads, padded_q, padded_k, head_dim, offset, query_length, key_length, float(scale),
         config.block_k, config.tile_q, float(config.alpha), config.sink_tokens,
         config.window_tokens, config.last_n_blocks, _lib.dtype_code(pdt), _lib.ptr(pooled_k),
         _lib.ptr(pooled_v), _lib.ptr(sel_ids), _lib.ptr(sel_counts), _lib.ptr(pr_ids),
-        _lib.ptr(pr_counts), _lib.ptr(mask), _lib.stream_of(q)))
+        _lib.ptr(pr_counts), _lib.ptr(mask), *_lib.workspace_args(ws), _lib.stream_of(q)))
     return (pooled_k, pooled_v, (sel_ids, sel_counts, pr_ids, pr_counts),
             None if mask is None else mask.view(torch.bool))
 

@@ -148,12 +148,13 @@ def block_scores_and_select(
     if config.score_chunk_tiles is None:
         raw = torch.empty((kv_heads, group, padded_length, num_blocks), dtype=torch.float32,
                           device=q.device)
+    ws = _lib.select_workspace(qc, kc.dtype, kv_heads, num_blocks, q.shape[-1])
     _lib.check(_lib.lib().fpv2_block_select(
         _lib.ptr(qc), _lib.dtype_code(q.dtype), _lib.ptr(kc), _lib.dtype_code(pooled_k.dtype),
         query_heads, kv_heads, padded_length, num_blocks, q.shape[-1], offset, valid_length,
         float(scale), config.block_k, config.tile_q, float(config.alpha), config.sink_tokens,
         config.window_tokens, config.last_n_blocks, _lib.ptr(mask), _lib.ptr(raw),
-        _lib.stream_of(q)))
+        *_lib.workspace_args(ws), _lib.stream_of(q)))
     return mask.view(torch.bool), raw
 
 

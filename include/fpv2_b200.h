@@ -85,6 +85,11 @@ FPV2_API int fpv2_pool_blocks(const void* x, int x_dtype, int64_t heads, int64_t
  * to causally visible blocks. `offset` is the absolute key position of query
  * row 0; rows >= query_length are padding. `raw_scores` (nullable) receives
  * the unmasked scale * q . pooled_k scores [kv_heads, G, padded_q_len, num_blocks].
+ * `workspace` (nullable, 256-byte aligned, `workspace_bytes` long): with
+ * float32 pooled keys and 16-bit queries, a workspace of
+ * fpv2_select_workspace_bytes() bytes holds the keys' three 16-bit parts so
+ * the tensor cores score them at float32 precision; without it those inputs
+ * are scored on the CUDA cores (same results).
  * Replaces fpv2/selection.py:109-201 (block_scores_and_select).
  */
 FPV2_API int fpv2_block_select(const void* q, int q_dtype, const void* pooled_k, int k_dtype,
@@ -93,7 +98,20 @@ FPV2_API int fpv2_block_select(const void* q, int q_dtype, const void* pooled_k,
                       int32_t query_length, float scale, int32_t block_k, int32_t tile_q,
                       float alpha, int32_t sink_tokens, int32_t window_tokens,
                       int32_t last_n_blocks, uint8_t* selected, float* raw_scores,
-                      void* stream);
+                      void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * Workspace bytes that let fpv2_block_select / fpv2_index_stage score float32
+ * pooled keys on the tensor cores (0 when the dtypes do not need any): three
+ * 16-bit parts of the keys, [3][kv_heads][num_blocks][head_dim] in the query
+ * dtype, and two ints per KV head (the head's largest magnitude and the
+ * power-of-two exponent that scales a head beyond the 16-bit range into it;
+ * the head's scores are scaled back). No
+ * counterpart in the reference (reference.py:45-51 scores float32 pooled keys
+ * with MLX's einsum).
+ */
+FPV2_API int64_t fpv2_select_workspace_bytes(int q_dtype, int k_dtype, int32_t kv_heads,
+                                    int32_t num_blocks, int32_t head_dim);
 
 /*
  * Mask -> padded block lists. selected_ids lists the selected blocks
@@ -113,7 +131,8 @@ FPV2_API int fpv2_compact_block_indices(const uint8_t* selected, int32_t kv_head
  * pooled_v (written as `pooled_dtype`: the input dtype, as fpv2/patch.py:137-138
  * pools, or FPV2_F32, as fpv2/reference.py:45-48 pools), selects on those
  * pooled keys and writes the four list/count arrays. `selected` (nullable)
- * also receives the mask.
+ * also receives the mask. `workspace` as for fpv2_block_select (used when
+ * pooled_dtype is FPV2_F32 and the inputs are 16-bit).
  * Replaces the pool_blocks x2 -> block_scores_and_select -> compact_block_indices
  * sequence of fpv2/patch.py:137-153.
  */
@@ -125,7 +144,8 @@ FPV2_API int fpv2_index_stage(const void* q, const void* k, const void* v, int d
                      int32_t window_tokens, int32_t last_n_blocks, int pooled_dtype,
                      void* pooled_k, void* pooled_v, int32_t* selected_ids,
                      int32_t* selected_counts, int32_t* pruned_ids, int32_t* pruned_counts,
-                     uint8_t* selected, void* stream);
+                     uint8_t* selected, void* workspace, int64_t workspace_bytes,
+                     void* stream);
 
 /*
  * Block-sparse attention over the lists: per query row, online softmax in

@@ -132,6 +132,78 @@ def test_selection_parity(case):
     assert chk.ok, chk
 
 
+SELECT_F32_CASES = [
+    # length, Hq, Hkv, D, q dtype, alpha, seed[, tile_q]: float32 pooled keys
+    (2048, 8, 2, 128, torch.bfloat16, 0.1, 30),
+    (2048, 8, 2, 128, torch.float16, 0.15, 31),
+    (2048, 16, 2, 128, torch.float16, 0.05, 32),     # G = 8, tile_q = 16
+    (2048, 8, 2, 64, torch.bfloat16, 0.1, 33),
+    (2048, 8, 2, 256, torch.bfloat16, 0.1, 34),
+    (2048, 8, 2, 128, torch.bfloat16, 0.1, 35, 256),
+]
+
+
+def _select_f32(qg, pk, scale, cfg, workspace):
+    """fpv2_block_select on float32 pooled keys with or without the split workspace
+    (without: the CUDA-core kernel)."""
+    hkv, nb, d = pk.shape
+    mask = torch.empty((hkv, qg.shape[1] // cfg.tile_q, nb), dtype=torch.uint8, device=DEV)
+    ws = _lib.select_workspace(qg, pk.dtype, hkv, nb, d) if workspace else None
+    assert (ws is not None) == workspace
+    _lib.check(_lib.lib().fpv2_block_select(
+        _lib.ptr(qg), _lib.dtype_code(qg.dtype), _lib.ptr(pk), _lib.dtype_code(pk.dtype),
+        qg.shape[0], hkv, qg.shape[1], nb, d, 0, qg.shape[1], float(scale), cfg.block_k,
+        cfg.tile_q, float(cfg.alpha), cfg.sink_tokens, cfg.window_tokens, cfg.last_n_blocks,
+        _lib.ptr(mask), None, *_lib.workspace_args(ws), _lib.stream_of(qg)))
+    return mask.cpu().numpy().astype(bool)
+
+
+@pytest.mark.parametrize("case", SELECT_F32_CASES,
+                         ids=lambda c: f"L{c[0]}-Hq{c[1]}-D{c[3]}-{c[4]}" + (f"-t{c[7]}" if len(c) > 7 else ""))
+def test_selection_parity_float32_pooled_keys(case):
+    """16-bit queries on float32 pooled keys (fpv2/reference.py:45-51 semantics):
+    the tensor-core kernel scores three 16-bit parts of each key; its selection
+    and the CUDA-core kernel's both match the float32 oracle."""
+    length, hq, hkv, d, dtype, alpha, seed = case[:7]
+    q, k, _ = topic_qkv(length=length, query_heads=hq, kv_heads=hkv, head_dim=d, seed=seed,
+                        dtype=dtype)
+    cfg = _effective_config(fpv2.FPV2Config(alpha=alpha, score_chunk_tiles=8), hq, hkv)
+    if len(case) > 7:
+        cfg = replace(cfg, tile_q=case[7])
+    pk_ref = O.pool_blocks(P.np32(k), 128, "fp32")
+    qg, pk = q.to(DEV), torch.from_numpy(pk_ref).to(DEV)
+    scale = d ** -0.5
+    sel, _ = fpv2.block_scores_and_select(qg, pk, scale=scale, config=cfg)
+    chk = P.check_selection(q, pk_ref, sel.cpu().numpy(), scale=scale, config=cfg)
+    assert chk.ok, chk
+    tc, cc = _select_f32(qg, pk, scale, cfg, True), _select_f32(qg, pk, scale, cfg, False)
+    assert np.array_equal(tc, sel.cpu().numpy())
+    chk = P.check_selection(q, pk_ref, cc, scale=scale, config=cfg)
+    assert chk.ok, chk
+    assert (tc != cc).mean() < 1e-3
+
+
+def test_selection_float32_pooled_keys_beyond_fp16_range():
+    """Pooled keys of 2^20 times ordinary magnitude with fp16 queries: the heads'
+    16-bit parts are scaled by 2^-e into range and scored at 2^e, so the selection
+    is that of the unscaled keys at scale * 2^-20 (exact in float32)."""
+    q, k, _ = topic_qkv(length=2048, query_heads=8, kv_heads=2, seed=36, dtype=torch.float16)
+    cfg = _effective_config(fpv2.FPV2Config(alpha=0.1, score_chunk_tiles=8), 8, 2)
+    pk_ref = O.pool_blocks(P.np32(k), 128, "fp32")
+    big = pk_ref * np.float32(2.0 ** 20)
+    assert np.abs(big).max() > 65504
+    scale = 128 ** -0.5
+    qg = q.to(DEV)
+    sel, _ = fpv2.block_scores_and_select(qg, torch.from_numpy(big).to(DEV),
+                                          scale=scale * 2.0 ** -20, config=cfg)
+    assert _lib.device_status() == 0
+    chk = P.check_selection(q, big, sel.cpu().numpy(), scale=scale * 2.0 ** -20, config=cfg)
+    assert chk.ok, chk
+    ref, _ = fpv2.block_scores_and_select(qg, torch.from_numpy(pk_ref).to(DEV), scale=scale,
+                                          config=cfg)
+    assert (sel != ref).float().mean().item() < 1e-3
+
+
 @pytest.mark.parametrize("offset,query_length", [(37, 55), (0, 160), (64, 96)])
 def test_selection_offset_and_padding(offset, query_length):
     """Chunk offsets and padded query rows (reference tests/test_selection.py:114-144)."""
