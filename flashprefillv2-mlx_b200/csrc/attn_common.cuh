@@ -92,5 +92,20 @@ __device__ __forceinline__ Chunk make_chunk(const Params& p, int w) {
 
 __device__ __forceinline__ int clampi(int x, int lo, int hi) { return min(max(x, lo), hi); }
 
+// Register budget of a warpgroup (setmaxnreg; all four warps execute it).
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// Bits 0 .. n-1 set (n clamped to [0, 32]).
+__device__ __forceinline__ uint32_t prefix_mask(long long n) {
+  return n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
+}
+
 }  // namespace
 }  // namespace fpv2

@@ -95,19 +95,6 @@ __device__ __forceinline__ Pair make_pair(const Params& p, int w) {
   return pr;
 }
 
-template <int N>
-__device__ __forceinline__ void regs_dec() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
-}
-template <int N>
-__device__ __forceinline__ void regs_inc() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
-}
-
-__device__ __forceinline__ uint32_t prefix_mask(long long n) {
-  return n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
-}
-
 // DT: input dtype; VT: operand type of the P.V product (V and P).
 template <int D, int DT, int VT>
 __global__ void __launch_bounds__(kThreads, 1)

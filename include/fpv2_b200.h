@@ -59,7 +59,9 @@ FPV2_API int fpv2_device_supported(int device);
 /*
  * Device status word of the current device. Kernels that give up a bounded
  * wait set a bit here instead of hanging; this call synchronises `stream`,
- * returns the word and clears it when `clear` is non-zero.
+ * returns the word and clears it when `clear` is non-zero. Bits: 1 a bounded
+ * wait expired, 2 TMEM allocation failed, 4 a split-work entry failed its
+ * bounds check.
  */
 FPV2_API int fpv2_device_status(void* stream, int clear, int32_t* status_out);
 
