@@ -243,3 +243,25 @@ def test_paged_api_validates_before_touching_the_gpu():
                                     ids, cnt, ids, cnt, scale=1.0)
     with pytest.raises(ValueError, match="identical shapes"):
         fpv2.sparse_attention_paged(q, cache, cache[:2], table, pk, pk, ids, cnt, ids, cnt, scale=1.0)
+
+
+def test_workspace_size_queries_without_gpu():
+    """The two workspace queries are pure size arithmetic (no device call)."""
+    L = _lib.lib()
+    hkv, nb, d = 8, 512, 128
+    # selection: three 16-bit parts of float32 pooled keys (+ two ints per KV head)
+    parts = 3 * hkv * nb * d * 2
+    got = L.fpv2_select_workspace_bytes(_lib.BF16, _lib.F32, hkv, nb, d)
+    assert got == (parts + 255) // 256 * 256 + 8 * hkv
+    assert L.fpv2_select_workspace_bytes(_lib.F16, _lib.F32, hkv, nb, d) == got
+    assert L.fpv2_select_workspace_bytes(_lib.BF16, _lib.BF16, hkv, nb, d) == 0   # 16-bit keys need none
+    assert L.fpv2_select_workspace_bytes(_lib.F32, _lib.F32, hkv, nb, d) == 0     # CUDA-core path
+    # attention: the fp16 copy of bf16 V (and pooled V) leads the split scratch
+    args = (32, hkv, 65536, 65536, d, 128, 32)
+    bf16 = L.fpv2_attention_workspace_bytes(_lib.BF16, *args, _lib.BF16, 1)
+    f16 = L.fpv2_attention_workspace_bytes(_lib.F16, *args, _lib.F16, 1)
+    up = lambda x: (x + 255) // 256 * 256
+    conv = up(hkv * 65536 * d * 2) + up(hkv * nb * d * 2) + up(hkv * 8)
+    assert bf16 - f16 == conv
+    assert f16 >= _lib.ATTN_WORKSPACE_BYTES
+    assert L.fpv2_attention_workspace_bytes(_lib.F32, *args, _lib.F32, 1) >= _lib.ATTN_WORKSPACE_BYTES
