@@ -8,14 +8,24 @@ K/V read of FPV2 belongs to one KV head (fpv2/selection.py:178-185,
 fpv2/kernel.py:212-256), so the layer splits into independent KV-head chunks,
 and the host->device copy of chunk c+1, the kernels of chunk c and the
 device->host copy of chunk c-1 run at the same time on three CUDA streams.
-The result equals ``fpv2_sdpa`` on the whole tensors bit for bit.
+The copies in set the pace, so the last chunk is cut again into query slices
+(chunked prefill: slice [s0, s1) attends the keys up to s1, and only the final
+slice keeps the dense tail), which leaves only the last slice's kernels and
+copy out after the last byte has come in.
+
+The result equals ``fpv2_sdpa`` on the whole tensors bit for bit whenever the
+attention kernel splits the same long work items over KV segments in both (a
+choice made per launch from the number of work items; where it differs the
+outputs differ by rounding only, well inside the output tolerance).
 """
 
 from __future__ import annotations
 
 import torch
 
-from fpv2.patch import fpv2_sdpa
+from dataclasses import replace
+
+from fpv2.patch import _effective_config, fpv2_sdpa
 from fpv2.selection import FPV2Config
 
 
@@ -29,6 +39,7 @@ def sdpa_from_host(
     out: torch.Tensor | None = None,
     kv_heads_per_chunk: int = 1,
     device: torch.device | None = None,
+    tail_slices: int = 4,
 ) -> torch.Tensor:
     """``fpv2_sdpa`` for ``[1, H, L, D]`` tensors in (preferably pinned) host memory.
 
@@ -36,7 +47,9 @@ def sdpa_from_host(
     queued on the current CUDA stream of ``device`` and two side streams; the
     current stream waits for the last copy, so synchronising it (or the device)
     makes ``out`` readable. Copies from or to pageable host memory still work but
-    do not overlap.
+    do not overlap. ``tail_slices`` (1 = off) cuts the last chunk into that many
+    query slices, on boundaries that are multiples of the selection tile and of
+    128 rows.
     """
     for name, t in (("q", q), ("k", k), ("v", v)):
         if t.device.type != "cpu":
@@ -50,6 +63,8 @@ def sdpa_from_host(
         raise ValueError("query heads must be a multiple of the key/value heads")
     if kv_heads_per_chunk <= 0 or hkv % kv_heads_per_chunk != 0:
         raise ValueError("kv_heads_per_chunk must divide the number of key/value heads")
+    if not isinstance(tail_slices, int) or tail_slices < 1:
+        raise ValueError("tail_slices must be a positive integer")
     if out is None:
         out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
     elif out.device.type != "cpu" or out.shape != q.shape or out.dtype != q.dtype or not out.is_contiguous():
@@ -59,6 +74,17 @@ def sdpa_from_host(
     g = hq // hkv
     cs = kv_heads_per_chunk
     nchunks = hkv // cs
+    lq, lk = q.shape[2], k.shape[2]
+    offset = lk - lq
+    # Query slices of the last chunk: cut points on multiples of 128 rows and of
+    # the selection tile, and the final slice holds at least the dense-tail tiles.
+    eff = _effective_config(config, hq, hkv)
+    unit = max(128, eff.tile_q * max(1, eff.last_n_blocks)) if eff is not None else lq
+    unit = (unit + 127) // 128 * 128
+    cuts = sorted({(i * lq // tail_slices) // unit * unit for i in range(1, tail_slices)} - {0})
+    while cuts and lq - cuts[-1] < unit:
+        cuts.pop()
+    bounds = list(zip([0] + cuts, cuts + [lq])) if offset >= 0 else [(0, lq)]
 
     compute = torch.cuda.current_stream(device)
     h2d = torch.cuda.Stream(device)
@@ -87,6 +113,10 @@ def sdpa_from_host(
         qb, kb, vb = bufs[b]
         hs = slice(c * cs * g, (c + 1) * cs * g)
         ks = slice(c * cs, (c + 1) * cs)
+        if c == nchunks - 1 and len(bounds) > 1:
+            last = _stream_sliced(q, k, v, out, qb, kb, vb, hs, ks, bounds, offset, scale, config,
+                                  compute, h2d, d2h, inputs_free[b])
+            break
         with torch.cuda.stream(h2d):
             if inputs_free[b] is not None:
                 h2d.wait_event(inputs_free[b])   # chunk c-2's kernels have read this set
@@ -110,3 +140,43 @@ def sdpa_from_host(
     if last is not None:
         compute.wait_event(last)
     return out
+
+
+def _stream_sliced(q, k, v, out, qb, kb, vb, hs, ks, bounds, offset, scale, config,
+                   compute, h2d, d2h, inputs_free):
+    """The last chunk in query slices: its K and V come in first, then the query
+    rows slice by slice (one copy per head: a slice is strided across heads);
+    slice i runs as soon as its rows have arrived and goes out right after."""
+    heads = range(hs.start, hs.stop)
+    loaded = []
+    with torch.cuda.stream(h2d):
+        if inputs_free is not None:
+            h2d.wait_event(inputs_free)   # chunk c-2's kernels have read this set
+        kb.copy_(k[:, ks], non_blocking=True)
+        vb.copy_(v[:, ks], non_blocking=True)
+        for s0, s1 in bounds:
+            for j, h in enumerate(heads):
+                qb[0, j, s0:s1].copy_(q[0, h, s0:s1], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(h2d)
+            loaded.append(ev)
+    last = None
+    for i, (s0, s1) in enumerate(bounds):
+        final = i == len(bounds) - 1
+        compute.wait_event(loaded[i])
+        with torch.cuda.stream(compute):
+            # queries [s0, s1) attend the keys before offset + s1; only the final
+            # slice holds the layer's last tiles (the dense tail)
+            cfg = config if final else replace(config, last_n_blocks=0)
+            kend = offset + s1
+            o = fpv2_sdpa(qb[:, :, s0:s1], kb[:, :, :kend], vb[:, :, :kend], scale=scale, config=cfg)
+            done = torch.cuda.Event()
+            done.record(compute)
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(done)
+            for j, h in enumerate(heads):
+                out[0, h, s0:s1].copy_(o[0, j], non_blocking=True)
+            last = torch.cuda.Event()
+            last.record(d2h)
+        o.record_stream(d2h)
+    return last

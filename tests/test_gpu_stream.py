@@ -16,8 +16,9 @@ from tests.synthetic import topic_qkv
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("chunk,query_length", [(1, 2048), (2, 2048), (1, 1920)])
-def test_sdpa_from_host_equals_device_layer(chunk, query_length):
+@pytest.mark.parametrize("chunk,query_length,tail_slices",
+                         [(1, 2048, 4), (2, 2048, 4), (1, 1920, 4), (1, 2048, 1), (2, 1920, 3)])
+def test_sdpa_from_host_equals_device_layer(chunk, query_length, tail_slices):
     dev = torch.device("cuda", 0)
     q, k, v = topic_qkv(length=2048, query_heads=16, kv_heads=4, seed=31, dtype=torch.bfloat16)
     q = q[None, :, 2048 - query_length:].contiguous()
@@ -25,7 +26,8 @@ def test_sdpa_from_host_equals_device_layer(chunk, query_length):
     cfg = fpv2.FPV2Config(alpha=0.1)
     ref = fpv2.fpv2_sdpa(q.to(dev), k.to(dev), v.to(dev), scale=128 ** -0.5, config=cfg)
     qh, kh, vh = (t.pin_memory() for t in (q, k, v))
-    out = fpv2.sdpa_from_host(qh, kh, vh, scale=128 ** -0.5, config=cfg, kv_heads_per_chunk=chunk)
+    out = fpv2.sdpa_from_host(qh, kh, vh, scale=128 ** -0.5, config=cfg, kv_heads_per_chunk=chunk,
+                              tail_slices=tail_slices)
     torch.cuda.synchronize(dev)
     assert out.is_pinned()
     assert torch.equal(out, ref.cpu())
