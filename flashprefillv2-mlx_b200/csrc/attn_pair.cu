@@ -235,8 +235,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int rows = min(a.page_size, 128);
             for (int r0 = 0; r0 < 128; r0 += rows) {
               const int key = rec.kstart + r0;
-              const int page = clampi(a.block_table[min(key / a.page_size, a.table_len - 1)], 0,
-                                      a.num_pages - 1);
+              const int page = clamp_entry(a.block_table[min(key / a.page_size, a.table_len - 1)],
+                                           0, a.num_pages - 1, p.status);
 #pragma unroll
               for (int hh = 0; hh < C::kHalves; ++hh)
                 tma_load_4d(dst + hh * 16384 + r0 * 128, m, bar, hh * 64, h, key % a.page_size,
@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const bool low = e >= 64;
           uint4 kvk = make_uint4(0, 0, 0, 0), kvv = make_uint4(0, 0, 0, 0);
           if (ent < rec.nvalid && cidx * 8 < a.D) {
-            const int blk = clampi(a.pr_ids[lrow + rec.kstart + ent], 0, a.Nb - 1);
+            const int blk = clamp_entry(a.pr_ids[lrow + rec.kstart + ent], 0, a.Nb - 1, p.status);
             const long long src = ((long long)h * a.Nb + blk) * a.D + cidx * 8;
             const float4* fk = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.pk) + src);
             const float4* fv = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.pv) + src);
@@ -306,14 +306,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = next_work(); w < p.items && ok; w = next_work()) {
       const Pair pr = make_pair(p, w);
       const long long lrow = ((long long)pr.h * a.Nt + pr.t) * a.Nb;
-      const int nsel = clampi(a.sel_counts[(long long)pr.h * a.Nt + pr.t], 0, a.Nb);
-      const int npr = a.corr ? clampi(a.pr_counts[(long long)pr.h * a.Nt + pr.t], 0, a.Nb) : 0;
+      const int nsel = clamp_entry(a.sel_counts[(long long)pr.h * a.Nt + pr.t], 0, a.Nb, p.status);
+      const int npr = a.corr ? clamp_entry(a.pr_counts[(long long)pr.h * a.Nt + pr.t], 0, a.Nb, p.status) : 0;
       // Selected blocks up to the first one past the chunks (fpv2/kernel.py:249-255).
       int n_sel_items = 0, brk = nsel;
       for (int i0 = 0; i0 < nsel; i0 += 32) {
         const int i = i0 + lane;
         const bool in = i < nsel;
-        const int blk = in ? clampi(a.sel_ids[lrow + i], 0, a.Nb - 1) : 0;
+        const int blk = in ? clamp_entry(a.sel_ids[lrow + i], 0, a.Nb - 1, p.status) : 0;
         const long long bstart = (long long)blk * a.block_k;
         const unsigned stop = __ballot_sync(0xffffffffu, in && bstart > pr.abs_last);
         const int lim = stop ? (__ffs(stop) - 1) : 32;
@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = lane; i < nwords; i += 32) pmask[i] = 0u;
         __syncwarp();
         for (int i = lane; i < npr; i += 32) {
-          const int blk = clampi(a.pr_ids[lrow + i], 0, a.Nb - 1);
+          const int blk = clamp_entry(a.pr_ids[lrow + i], 0, a.Nb - 1, p.status);
           atomicOr(&pmask[blk >> 5], 1u << (blk & 31));
         }
         __syncwarp();
@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       for (int i0 = 0; i0 < brk && ok; i0 += 32) {
         const int i = i0 + lane;
-        const int blk = i < brk ? clampi(a.sel_ids[lrow + i], 0, a.Nb - 1) : 0;
+        const int blk = i < brk ? clamp_entry(a.sel_ids[lrow + i], 0, a.Nb - 1, p.status) : 0;
         const int cnt = min(32, brk - i0);
         for (int j = 0; j < cnt && ok; ++j) {
           const int bj = __shfl_sync(0xffffffffu, blk, j);

@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
             const bool low = e >= 64;
             uint4 val = make_uint4(0, 0, 0, 0);
             if (ent < rec.nvalid) {
-              const int blk = clampi(a.pr_ids[lrow + rec.kstart + ent], 0, a.Nb - 1);
+              const int blk = clamp_entry(a.pr_ids[lrow + rec.kstart + ent], 0, a.Nb - 1, p.status);
               const long long src = ((long long)ck.h * a.Nb + blk) * kD + cidx * 8;
               const float4* f = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src_base) + src);
               const float4 x0 = __ldg(f), x1 = __ldg(f + 1);
@@ -243,8 +243,8 @@ __global__ void __launch_bounds__(kWThreads, 1)
     for (int w = next_work(); w < p.items && ok; w = next_work()) {
       const Chunk ck = make_chunk(p, w);
       const long long lrow = ((long long)ck.h * a.Nt + ck.t) * a.Nb;
-      const int nsel = clampi(a.sel_counts[(long long)ck.h * a.Nt + ck.t], 0, a.Nb);
-      const int npr = a.corr ? clampi(a.pr_counts[(long long)ck.h * a.Nt + ck.t], 0, a.Nb) : 0;
+      const int nsel = clamp_entry(a.sel_counts[(long long)ck.h * a.Nt + ck.t], 0, a.Nb, p.status);
+      const int npr = a.corr ? clamp_entry(a.pr_counts[(long long)ck.h * a.Nt + ck.t], 0, a.Nb, p.status) : 0;
       first_v = true;
       // Q tile of the chunk (its buffer frees when the previous item's last QK completes).
       if (lane == 0) ok = mbar_wait(smem_u32(q_empty), (qcount & 1) ^ 1, wc);
@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
       for (int i0 = 0; i0 < nsel; i0 += 32) {
         const int i = i0 + lane;
         const bool in = i < nsel;
-        const int blk = in ? clampi(a.sel_ids[lrow + i], 0, a.Nb - 1) : 0;
+        const int blk = in ? clamp_entry(a.sel_ids[lrow + i], 0, a.Nb - 1, p.status) : 0;
         const long long bstart = (long long)blk * a.block_k;
         const unsigned stop = __ballot_sync(0xffffffffu, in && bstart > ck.abs_last);
         const int lim = stop ? (__ffs(stop) - 1) : 32;
@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
         for (int i = lane; i < nwords; i += 32) pmask[i] = 0u;
         __syncwarp();
         for (int i = lane; i < npr; i += 32) {
-          const int blk = clampi(a.pr_ids[lrow + i], 0, a.Nb - 1);
+          const int blk = clamp_entry(a.pr_ids[lrow + i], 0, a.Nb - 1, p.status);
           atomicOr(&pmask[blk >> 5], 1u << (blk & 31));
         }
         __syncwarp();
@@ -311,7 +311,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
       };
       for (int i0 = 0; i0 < brk && ok; i0 += 32) {
         const int i = i0 + lane;
-        const int blk = i < brk ? clampi(a.sel_ids[lrow + i], 0, a.Nb - 1) : 0;
+        const int blk = i < brk ? clamp_entry(a.sel_ids[lrow + i], 0, a.Nb - 1, p.status) : 0;
         const int cnt = min(32, brk - i0);
         for (int j = 0; j < cnt && ok; ++j) {
           const int bj = __shfl_sync(0xffffffffu, blk, j);

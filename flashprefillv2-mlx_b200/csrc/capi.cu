@@ -522,6 +522,7 @@ int run_sparse_attention(const void* q, const void* k, const void* v, const void
   a.scale_log2 = scale * kLog2e;
   a.corr_shift = (float)log2((double)block_k);
   a.out_mc = out_mc;
+  a.status = d->status;
   a.mc_head_offset = head_offset;
   a.mc_heads = heads_total;
   if (paged != nullptr) {

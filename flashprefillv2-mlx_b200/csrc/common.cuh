@@ -22,7 +22,25 @@ enum : int {
   STATUS_TIMEOUT = 1,      // a bounded wait expired
   STATUS_TMEM_ALLOC = 2,   // TMEM allocation returned an unusable address
   STATUS_BAD_SPLIT = 4,    // a split-queue entry or partial slot failed its bounds check
+  STATUS_BAD_LIST = 8,     // (FPV2_DEBUG_BOUNDS builds) a list entry or count was out of range
 };
+
+#ifndef FPV2_DEBUG_BOUNDS
+#define FPV2_DEBUG_BOUNDS 0
+#endif
+
+// A block-list entry, count or page index clamped into [lo, hi], as the
+// reference clips its lists (fpv2/kernel.py:555-558). A build with
+// FPV2_DEBUG_BOUNDS=1 also reports every value that needed the clamp in the
+// status word (STATUS_BAD_LIST) instead of trapping.
+__device__ __forceinline__ int clamp_entry(int v, int lo, int hi, int* status) {
+#if FPV2_DEBUG_BOUNDS
+  if ((v < lo || v > hi) && status != nullptr) atomicOr(status, STATUS_BAD_LIST);
+#else
+  (void)status;
+#endif
+  return min(max(v, lo), hi);
+}
 
 constexpr float kFiniteMin = -3.402823466e+38f;  // Metal's Limits<float>::finite_min
 constexpr float kLog2e = 1.4426950408889634f;

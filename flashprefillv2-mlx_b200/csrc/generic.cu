@@ -261,9 +261,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_generic_kernel(AttnArgs 
   for (int i = 0; i < kMaxDPerLane; ++i) o[i] = 0.f;
   float m_run = kFiniteMin, l_run = 0.f;
 
-  const int nsel = min(max(a.sel_counts[(long long)h * a.Nt + t], 0), a.Nb);
+  const int nsel = clamp_entry(a.sel_counts[(long long)h * a.Nt + t], 0, a.Nb, a.status);
   for (int i = 0; i < nsel; ++i) {
-    const int blk = min(max(a.sel_ids[list_row + i], 0), a.Nb - 1);
+    const int blk = clamp_entry(a.sel_ids[list_row + i], 0, a.Nb - 1, a.status);
     const long long bstart = (long long)blk * a.block_k;
     if (bstart > abs_last) break;
     for (int k0 = 0; k0 < a.block_k; k0 += 32) {
@@ -298,11 +298,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_generic_kernel(AttnArgs 
     }
   }
   if (a.corr) {
-    const int npr = min(max(a.pr_counts[(long long)h * a.Nt + t], 0), a.Nb);
+    const int npr = clamp_entry(a.pr_counts[(long long)h * a.Nt + t], 0, a.Nb, a.status);
     for (int e0 = 0; e0 < npr; e0 += 32) {
       const int e = e0 + lane;
       const bool in = e < npr;
-      const int blk = min(max(a.pr_ids[list_row + (in ? e : e0)], 0), a.Nb - 1);
+      const int blk = clamp_entry(a.pr_ids[list_row + (in ? e : e0)], 0, a.Nb - 1, a.status);
       float s = kFiniteMin;
       if (in) {
         float acc = 0.f;

@@ -97,6 +97,7 @@ struct AttnArgs {
   const void* v_conv = nullptr;
   const void* pv_conv = nullptr;
   const int* v_exp = nullptr;
+  int* status = nullptr;   // device status word (list bounds reports of debug builds)
 };
 
 // ---- V -> fp16 copy for the P.V product (convert.cu) -------------------------

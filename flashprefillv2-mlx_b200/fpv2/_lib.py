@@ -7,12 +7,17 @@ CUDA tensor, the operators raise instead of falling back to anything else.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libfpv2_b200.so"
+# FPV2_LIBRARY selects another build of the library (e.g. libfpv2_b200_debug.so,
+# whose kernels report clamped list entries in the device status word).
+LIB_PATH = Path(os.environ.get("FPV2_LIBRARY") or
+                Path(__file__).resolve().parent / "_lib" / "libfpv2_b200.so")
+STATUS_BAD_LIST = 8   # device status bit of the debug build's list bounds reports
 
 F16, BF16, F32 = 0, 1, 2
 OK = 0

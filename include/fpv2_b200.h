@@ -61,7 +61,9 @@ FPV2_API int fpv2_device_supported(int device);
  * wait set a bit here instead of hanging; this call synchronises `stream`,
  * returns the word and clears it when `clear` is non-zero. Bits: 1 a bounded
  * wait expired, 2 TMEM allocation failed, 4 a split-work entry failed its
- * bounds check.
+ * bounds check, 8 (debug builds only, `build.py --debug-bounds`) a block-list
+ * entry, count or page index was out of range; kernels clamp such values into
+ * range in every build, as the reference clips its lists.
  */
 FPV2_API int fpv2_device_status(void* stream, int clear, int32_t* status_out);
 
