@@ -51,12 +51,20 @@ __device__ __forceinline__ void convert_head(const VConvArgs& a, int h, float sc
   const int vec_row = a.D / 8;
   const long long nvec = (long long)a.L * vec_row;
   uint4* dst = reinterpret_cast<uint4*>(a.v16) + (long long)h * nvec;
-  for (long long i = (long long)blockIdx.x * kConvThreads + threadIdx.x; i < nvec;
-       i += (long long)gridDim.x * kConvThreads) {
-    const long long row = i / vec_row;
-    const int col = (int)(i % vec_row) * 8;
-    dst[i] = conv8(__ldg(v_src(a, h, row, col)), scale, amax);
+  const long long stride = (long long)gridDim.x * kConvThreads;
+  long long i = (long long)blockIdx.x * kConvThreads + threadIdx.x;
+  // four independent 16-byte loads in flight per thread before converting them
+  for (; i + 3 * stride < nvec; i += 4 * stride) {
+    uint4 x[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long j = i + u * stride;
+      x[u] = __ldg(v_src(a, h, j / vec_row, (int)(j % vec_row) * 8));
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) dst[i + u * stride] = conv8(x[u], scale, amax);
   }
+  for (; i < nvec; i += stride) dst[i] = conv8(__ldg(v_src(a, h, i / vec_row, (int)(i % vec_row) * 8)), scale, amax);
   if (a.pv != nullptr && blockIdx.x == 0) {   // pooled V: means of V, so within the same range
     const long long npv = (long long)a.Nb * vec_row;
     const uint4* src = reinterpret_cast<const uint4*>(a.pv) + (long long)h * npv;
