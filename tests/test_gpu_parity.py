@@ -139,6 +139,7 @@ SELECT_F32_CASES = [
     (2048, 16, 2, 128, torch.float16, 0.05, 32),     # G = 8, tile_q = 16
     (2048, 8, 2, 64, torch.bfloat16, 0.1, 33),
     (2048, 8, 2, 256, torch.bfloat16, 0.1, 34),
+    (2048, 8, 2, 96, torch.bfloat16, 0.1, 37),       # zero-padded 128-wide tiles
     (2048, 8, 2, 128, torch.bfloat16, 0.1, 35, 256),
 ]
 
