@@ -500,20 +500,25 @@ def _attention_with_workspace(q, k, v, pk, pv, lists, cfg, scale, nbytes):
     return out
 
 
-def test_long_items_split_over_segments():
+@pytest.mark.parametrize("head_dim,dtype", [(128, torch.bfloat16), (64, torch.bfloat16),
+                                            (96, torch.float16)])
+def test_long_items_split_over_segments(head_dim, dtype):
     """At 32k the dense-tail tiles walk 256 key blocks: with the full workspace they
     are split into segments whose partial results a combine kernel merges. The
-    split layer agrees with the unsplit one (same fp16 product, workspace without
-    the split scratch) to within rounding, and with the float32 math."""
-    length, hq, hkv = 32768, 8, 2
-    q, k, v = topic_qkv(length=length, query_heads=hq, kv_heads=hkv, seed=61, dtype=torch.bfloat16)
+    split layer agrees with the unsplit one (same P.V precision, workspace without
+    the split scratch) to within rounding, and with the float32 math. Head dims
+    64 and 96 (128-wide tiles) exercise the other partial-slot widths, fp16 the
+    path without the V copy."""
+    length, hq, hkv, d = 32768, 8, 2, head_dim
+    q, k, v = topic_qkv(length=length, query_heads=hq, kv_heads=hkv, head_dim=d, seed=61, dtype=dtype)
     cfg = _effective_config(fpv2.FPV2Config(alpha=0.1), hq, hkv)
-    scale = 128 ** -0.5
+    scale = d ** -0.5
     qg, kg, vg = cuda(q, k, v)
     pk, pv, lists, mask = fpv2.index_stage(qg, kg, vg, scale=scale, config=cfg, offset=0,
                                            query_length=length, key_length=length, return_mask=True)
-    full = _lib.lib().fpv2_attention_workspace_bytes(
-        _lib.BF16, hq, hkv, length, length, 128, 128, cfg.tile_q, _lib.BF16, 1)
+    code = _lib.dtype_code(dtype)
+    full = _lib.lib().fpv2_attention_workspace_bytes(code, hq, hkv, length, length, d, 128,
+                                                     cfg.tile_q, code, 1)
     nt = length // cfg.tile_q
     split = _attention_with_workspace(qg, kg, vg, pk, pv, lists, cfg, scale, full)
     default = fpv2.sparse_attention(qg, kg, vg, pk, pv, *lists, scale=scale, config=cfg)
@@ -521,8 +526,10 @@ def test_long_items_split_over_segments():
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
     nb = length // 128
-    v_copy = ((hkv * length * 128 * 2 + 255) // 256 * 256 + (hkv * nb * 128 * 2 + 255) // 256 * 256
-              + (hkv * 8 + 255) // 256 * 256)
+    v_copy = 0
+    if dtype == torch.bfloat16:
+        v_copy = ((hkv * length * d * 2 + 255) // 256 * 256 + (hkv * nb * d * 2 + 255) // 256 * 256
+                  + (hkv * 8 + 255) // 256 * 256)
     unsplit = _attention_with_workspace(qg, kg, vg, pk, pv, lists, cfg, scale, v_copy + 4096)
     mx, mean = P.kernel_errors(split, P.np32(unsplit))
     assert mx <= 2 ** -7 and mean <= 1e-5, (mx, mean)
