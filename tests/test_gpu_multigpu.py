@@ -82,7 +82,10 @@ def _worker(rank: int, world: int, port: int, length: int, hq: int, hkv: int, d:
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("length,hq,hkv,d", [(8192, 32, 8, 128), (4096 + 384, 16, 4, 128),
-                                             (4096, 8, 2, 256), (4096, 8, 2, 96)])
+                                             (4096, 8, 2, 256), (4096, 8, 2, 96),
+                                             # dense-tail tiles of 256 blocks: split items, whose
+                                             # merged output leaves through the combine kernel
+                                             (32768, 16, 4, 128)])
 def test_head_parallel_two_gpus_matches_single_gpu(length, hq, hkv, d):
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
