@@ -500,25 +500,28 @@ def _attention_with_workspace(q, k, v, pk, pv, lists, cfg, scale, nbytes):
     return out
 
 
-@pytest.mark.parametrize("head_dim,dtype", [(128, torch.bfloat16), (64, torch.bfloat16),
-                                            (96, torch.float16)])
-def test_long_items_split_over_segments(head_dim, dtype):
+@pytest.mark.parametrize("head_dim,dtype,pooled", [(128, torch.bfloat16, None), (64, torch.bfloat16, None),
+                                                   (96, torch.float16, None),
+                                                   (128, torch.bfloat16, torch.float32)])
+def test_long_items_split_over_segments(head_dim, dtype, pooled):
     """At 32k the dense-tail tiles walk 256 key blocks: with the full workspace they
     are split into segments whose partial results a combine kernel merges. The
     split layer agrees with the unsplit one (same P.V precision, workspace without
     the split scratch) to within rounding, and with the float32 math. Head dims
     64 and 96 (128-wide tiles) exercise the other partial-slot widths, fp16 the
-    path without the V copy."""
+    path without the V copy, float32 pooled inputs the gathered high/low
+    correction items of fpv2/reference.py's semantics."""
     length, hq, hkv, d = 32768, 8, 2, head_dim
     q, k, v = topic_qkv(length=length, query_heads=hq, kv_heads=hkv, head_dim=d, seed=61, dtype=dtype)
     cfg = _effective_config(fpv2.FPV2Config(alpha=0.1), hq, hkv)
     scale = d ** -0.5
     qg, kg, vg = cuda(q, k, v)
     pk, pv, lists, mask = fpv2.index_stage(qg, kg, vg, scale=scale, config=cfg, offset=0,
-                                           query_length=length, key_length=length, return_mask=True)
+                                           query_length=length, key_length=length, return_mask=True,
+                                           pooled_dtype=pooled)
     code = _lib.dtype_code(dtype)
     full = _lib.lib().fpv2_attention_workspace_bytes(code, hq, hkv, length, length, d, 128,
-                                                     cfg.tile_q, code, 1)
+                                                     cfg.tile_q, _lib.dtype_code(pk.dtype), 1)
     nt = length // cfg.tile_q
     split = _attention_with_workspace(qg, kg, vg, pk, pv, lists, cfg, scale, full)
     default = fpv2.sparse_attention(qg, kg, vg, pk, pv, *lists, scale=scale, config=cfg)
@@ -535,7 +538,8 @@ def test_long_items_split_over_segments(head_dim, dtype):
     assert mx <= 2 ** -7 and mean <= 1e-5, (mx, mean)
     tiles = [0, nt // 2, nt - 3, nt - 2, nt - 1]
     ref = O.fpv2_attention_blockwise(P.np32(q), P.np32(k), P.np32(v), scale=scale, config=cfg,
-                                     selected=mask.cpu().numpy(), pooled_dtype="bf16",
+                                     selected=mask.cpu().numpy(),
+                                     pooled_dtype="fp32" if pooled is not None else P.dtname(dtype),
                                      tiles=[(h, t) for h in range(hkv) for t in tiles])
     pos = P.tile_positions(tiles, cfg.tile_q, length)
     err = np.abs(P.rows_of(split, pos) - ref[:, pos])
