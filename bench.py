@@ -270,6 +270,10 @@ def parse_args(argv=None):
     ap.add_argument("--config", choices=sorted(CONFIGS) + ["c4"], default="c3",
                     help="c4: chunked 64k prefill through a random-init Qwen3-4B-architecture model")
     ap.add_argument("--c4-layers", type=int, default=36, help="decoder layers of the c4 model")
+    ap.add_argument("--c4-qk-gain", type=float, default=1.0,
+                    help="c4: value of the per-head q/k RMSNorm weights (random init leaves them "
+                         "at 1, logits of std ~1, so alpha keeps every block; a gain g scales the "
+                         "logits by g^2, giving the peaked attention a trained model has)")
     ap.add_argument("--no-corr", action="store_true", help="mean correction off")
     ap.add_argument("--alpha", type=float, default=None)
     ap.add_argument("--tile-q", type=int, default=None,
@@ -304,9 +308,10 @@ def dist_setup(n: int):
 # ---------------------------------------------------------------------------
 
 
-def _qwen3_weights(dev, layers, seed=0):
+def _qwen3_weights(dev, layers, seed=0, qk_gain=1.0):
     """Random bf16 weights ~ N(0, 0.02) of the Qwen3-4B architecture (hidden 2560,
-    32 Q / 8 KV heads of 128, SwiGLU 9728, RMSNorm with per-head q/k norms)."""
+    32 Q / 8 KV heads of 128, SwiGLU 9728, RMSNorm with per-head q/k norms whose
+    weights are ``qk_gain``)."""
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
 
@@ -315,8 +320,9 @@ def _qwen3_weights(dev, layers, seed=0):
 
     H, I, HQ, HKV, D, V = 2560, 9728, 32, 8, 128, 151936
     ones = lambda n: torch.ones(n, device=dev, dtype=torch.bfloat16)  # noqa: E731
-    blocks = [dict(ln1=ones(H), wq=w(HQ * D, H), wk=w(HKV * D, H), wv=w(HKV * D, H), qn=ones(D),
-                   kn=ones(D), wo=w(H, HQ * D), ln2=ones(H), wg=w(I, H), wu=w(I, H), wd=w(H, I))
+    blocks = [dict(ln1=ones(H), wq=w(HQ * D, H), wk=w(HKV * D, H), wv=w(HKV * D, H),
+                   qn=ones(D) * qk_gain, kn=ones(D) * qk_gain, wo=w(H, HQ * D), ln2=ones(H),
+                   wg=w(I, H), wu=w(I, H), wd=w(H, I))
               for _ in range(layers)]
     return dict(embed=w(V, H), blocks=blocks, norm=ones(H), lm_head=w(V, H))
 
@@ -388,7 +394,7 @@ def c4_prefill(args) -> int:
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     L, chunk = 65536, 2048
-    weights = _qwen3_weights(dev, args.c4_layers)
+    weights = _qwen3_weights(dev, args.c4_layers, qk_gain=args.c4_qk_gain)
     g = torch.Generator(device=dev)
     g.manual_seed(1)
     ids = torch.randint(0, 151936, (L,), device=dev, generator=g)
@@ -422,6 +428,7 @@ def c4_prefill(args) -> int:
         "data": "random-init weights ~ N(0, 0.02), token ids uniform over the 151936 vocab (seed 1)",
         "config": {"workload": f"c4: {L} tokens in {chunk}-token chunks, total_tokens={L}, "
                                f"{args.c4_layers} layers, alpha=0.1, min_tokens=4096",
+                   "qk_norm_gain": args.c4_qk_gain,
                    "dense_prefill_s": round(times["dense"], 3),
                    "fpv2_prefill_s": round(times["fpv2"], 3),
                    "speedup_vs_dense": round(times["dense"] / times["fpv2"], 3),
