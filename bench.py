@@ -658,15 +658,15 @@ def main(argv=None) -> int:
         out_p = fpv2.sparse_attention(qd[0], kd[0], vd[0], pk_p, pv_p, *lists_p, scale=scale,
                                       config=cfg)
         torch.cuda.synchronize()
-        torch.set_num_threads(os.cpu_count() or 1)
         dt, fl, descs, samples = 0.0, 0.0, [], []
-        for head in range(min(args.cpu_heads, Hkv)):   # about 10 s of host work by default
-            d_h, f_h, desc_h, smp = cpu_sample(q, k, v, cfg, tiles_per_step=args.cpu_tiles,
-                                               head=head, want_outputs=True)
-            dt += d_h
-            fl += f_h
-            descs.append(desc_h)
-            samples.append(smp)
+        with all_host_threads():
+            for head in range(min(args.cpu_heads, Hkv)):   # about 10 s of host work by default
+                d_h, f_h, desc_h, smp = cpu_sample(q, k, v, cfg, tiles_per_step=args.cpu_tiles,
+                                                   head=head, want_outputs=True)
+                dt += d_h
+                fl += f_h
+                descs.append(desc_h)
+                samples.append(smp)
         cpu = {"value": round(fl / dt / 1e12, 6), "unit": "TFLOP/s", "cores": os.cpu_count(),
                "kind": "port", "sample": "; ".join(descs), "seconds": round(dt, 2)}
         parity = sample_parity(samples, lists_p, out_p, G, cfg.tile_q)
@@ -756,21 +756,30 @@ def main(argv=None) -> int:
     return 0
 
 
+def all_host_threads():
+    """Every host core for the CPU legs: torch's pool and NumPy's BLAS pool (which
+    follows OMP_NUM_THREADS, set to 1 per rank by torch.distributed.run)."""
+    from threadpoolctl import threadpool_limits
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    return threadpool_limits(limits=os.cpu_count() or 1)
+
+
 def reference_arm(args, length, Hq, Hkv, D, dtype, cfg) -> int:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     from tests.synthetic import topic_qkv
 
-    torch.set_num_threads(os.cpu_count() or 1)
     q, k, v = topic_qkv(length=length, query_heads=Hq, kv_heads=Hkv, head_dim=D, seed=0, dtype=dtype)
-    for _ in range(max(3, args.warmup)):
-        cpu_sample(q, k, v, cfg, tiles_per_step=max(8, args.cpu_tiles // 8))
     times, flops, desc = [], [], ""
-    for _ in range(args.steps):
-        dt, fl, desc = cpu_sample(q, k, v, cfg, tiles_per_step=max(8, args.cpu_tiles // 8))
-        times.append(dt)
-        flops.append(fl)
+    with all_host_threads():
+        for _ in range(max(3, args.warmup)):
+            cpu_sample(q, k, v, cfg, tiles_per_step=max(8, args.cpu_tiles // 8))
+        for _ in range(args.steps):
+            dt, fl, desc = cpu_sample(q, k, v, cfg, tiles_per_step=max(8, args.cpu_tiles // 8))
+            times.append(dt)
+            flops.append(fl)
     value = sum(flops) / sum(times) / 1e12
     ms = 1e3 * sum(times) / len(times)
     line = {
