@@ -699,10 +699,7 @@ def main(argv=None) -> int:
             "dtype": "bf16" if dtype == torch.bfloat16 else "fp16",
             "data": "synthetic topic-block generator (seed 0), inputs resident in HBM",
             "config": {
-                "workload": f"{args.config}: FPV2 layer L={length}, Hq={Hq}, Hkv={Hkv}, head_dim={D}, "
-                            f"alpha={alpha}, correction={'on' if cfg.mean_correction else 'off'}, "
-                            f"sink_tokens={cfg.sink_tokens}, window_tokens={cfg.window_tokens}, "
-                            f"last_n_blocks={cfg.last_n_blocks}, tile_q={cfg.tile_q} ({G * cfg.tile_q} packed rows)",
+                "workload": layer_workload(args, length, Hq, Hkv, D, cfg),
                 "parallelism": (f"head-parallel x{world}, output reassembled by NVLink multicast "
                                 "stores from the attention kernel" if mc is not None else
                                 f"head-parallel x{world} (+NCCL all-gather of the output)") if world > 1
@@ -756,6 +753,14 @@ def main(argv=None) -> int:
     return 0
 
 
+def layer_workload(args, length, Hq, Hkv, D, cfg) -> str:
+    """The workload both arms name in ``config``: one FPV2 layer of this shape."""
+    return (f"{args.config}: FPV2 layer L={length}, Hq={Hq}, Hkv={Hkv}, head_dim={D}, "
+            f"alpha={cfg.alpha}, correction={'on' if cfg.mean_correction else 'off'}, "
+            f"sink_tokens={cfg.sink_tokens}, window_tokens={cfg.window_tokens}, "
+            f"last_n_blocks={cfg.last_n_blocks}, tile_q={cfg.tile_q} ({(Hq // Hkv) * cfg.tile_q} packed rows)")
+
+
 def all_host_threads():
     """Every host core for the CPU legs: torch's pool and NumPy's BLAS pool (which
     follows OMP_NUM_THREADS, set to 1 per rank by torch.distributed.run)."""
@@ -788,11 +793,11 @@ def reference_arm(args, length, Hq, Hkv, D, dtype, cfg) -> int:
         "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16" if dtype == torch.bfloat16 else "fp16",
         "data": "synthetic topic-block generator (seed 0)",
-        "config": {"workload": f"{args.config}: FPV2 layer L={length}, Hq={Hq}, Hkv={Hkv}, head_dim={D}, "
-                               f"alpha={cfg.alpha}, correction={'on' if cfg.mean_correction else 'off'}; "
-                               "CPU port of the reference algorithm on a bounded sample per step"},
+        "config": {"workload": layer_workload(args, length, Hq, Hkv, D, cfg)},
         "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": os.cpu_count(),
-                         "kind": "port", "sample": desc},
+                         "kind": "port",
+                         "sample": f"CPU port of the reference algorithm on a bounded sample of this "
+                                   f"workload per step: {desc}"},
         "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
