@@ -6,8 +6,9 @@ topic-block synthetic inputs): the fused index stage (pool K/V, score, select,
 compact) followed by the tcgen05 sparse attention, through the public
 ``fpv2.fpv2_sdpa`` call with inputs resident in HBM. With N > 1 GPUs the layer
 is split head-parallel (Hkv/N KV heads and their query heads per GPU) and the
-output is re-assembled with one NCCL all-gather; total work is fixed (strong
-scaling) and ``value`` is the whole layer's retained TFLOP/s.
+attention kernel re-assembles the output on every rank with NVLink multicast
+stores (one NCCL all-gather where the GPUs offer no multicast); total work is
+fixed (strong scaling) and ``value`` is the whole layer's retained TFLOP/s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
@@ -222,15 +223,44 @@ def cpu_sample(q, k, v, cfg, *, tiles_per_step: int, head: int = 0, seed_tile: i
             f"list-driven attention, numpy float32")
     if not want_outputs:
         return dt, flops, desc
-    return dt, flops, desc, dict(head=head, row0=row0, tiles=tiles, lists=lists, out=out)
+    return dt, flops, desc, dict(head=head, row0=row0, tiles=tiles, lists=lists, out=out, pk=pk,
+                                 scale=D ** -0.5)
 
 
-def sample_parity(samples, lists_gpu, out_gpu, G: int, tile_q: int) -> dict:
+def _tile_flip(q, smp, t: int, gpu_tile, cfg, nt: int, G: int) -> bool:
+    """True when tile ``t``'s GPU lists differ from the oracle's only by blocks whose
+    float64 energy lies within 1e-5 relative of the alpha threshold, and are the
+    exact compaction of the GPU's own selection (north_star's allowed flips)."""
+    from oracle import fpv2_oracle as O
+
+    h, tq = smp["head"], cfg.tile_q
+    rows = q[h * G:(h + 1) * G, t * tq:(t + 1) * tq].float().numpy()
+    c = replace(O.as_config(cfg), score_chunk_tiles=None,
+                last_n_blocks=1 if t >= nt - cfg.last_n_blocks else 0)
+    kw = dict(scale=smp["scale"], config=c, offset=t * tq)
+    r32 = O.block_scores_and_select(rows, smp["pk"], **kw)
+    r64 = O.block_scores_and_select(rows, smp["pk"], precision="fp64", **kw)
+    band = O.threshold_band(r64)[0, 0]
+    ids, counts = gpu_tile[0][0, 0], int(gpu_tile[1][0, 0])
+    gpu_mask = np.zeros_like(r32.selected[0, 0])
+    gpu_mask[ids[:counts]] = True
+    diff = gpu_mask != r32.selected[0, 0]
+    if not diff.any() or (diff & ~band).any():
+        return False
+    ref = O.compact_block_indices(gpu_mask[None, None], config=c, offset=t * tq,
+                                  query_length=tq, key_length=q.shape[1])
+    return all(np.array_equal(a, b) for a, b in zip(gpu_tile, ref))
+
+
+def sample_parity(samples, lists_gpu, out_gpu, G: int, q, cfg) -> dict:
     """GPU lists and output of the CPU sample's tiles vs the oracle's: full-width
-    lists bit-exact per tile (an in-band threshold flip shows as a mismatched
-    tile) and the output within max-abs 2e-2 / mean-abs 2e-3 of the float32
-    list-driven math (outside the timed region)."""
-    tiles_total = mismatched = 0
+    lists bit-exact per tile except threshold flips (blocks whose float64 energy
+    lies within 1e-5 relative of alpha * max, reported as in-band flips), and
+    the output within max-abs 2e-2 / mean-abs 2e-3 of the float32 list-driven
+    math (outside the timed region)."""
+    tile_q = cfg.tile_q
+    nt = q.shape[1] // tile_q
+    tiles_total = mismatched = in_band = 0
     mx, sum_abs, n = 0.0, 0.0, 0
     for smp in samples:
         h, tiles = smp["head"], smp["tiles"]
@@ -241,7 +271,10 @@ def sample_parity(samples, lists_gpu, out_gpu, G: int, tile_q: int) -> dict:
             same = (got == exp).reshape(t1 - t0, -1).all(axis=1)
             equal &= same
         tiles_total += t1 - t0
-        mismatched += int((~equal).sum())
+        for i in np.nonzero(~equal)[0]:
+            mismatched += 1
+            tile = [x[:, i:i + 1] for x in gpu_lists]
+            in_band += int(_tile_flip(q, smp, t0 + int(i), tile, cfg, nt, G))
         r0, r1 = t0 * tile_q, t1 * tile_q
         o = out_gpu[h * G:(h + 1) * G, r0:r1].to("cpu", torch.float32).numpy()
         err = np.abs(o - smp["out"][:, :r1 - r0])
@@ -250,10 +283,13 @@ def sample_parity(samples, lists_gpu, out_gpu, G: int, tile_q: int) -> dict:
         n += err.size
     mean = sum_abs / max(n, 1)
     return {"tiles_checked": tiles_total, "tiles_with_list_mismatch": mismatched,
+            "tiles_with_in_band_flip": in_band, "tiles_out_of_band": mismatched - in_band,
             "max_abs": round(mx, 6), "mean_abs": round(mean, 7),
-            "ok": bool(mismatched == 0 and mx <= 2e-2 and mean <= 2e-3),
-            "criterion": "full-width lists bit-exact per tile; output max-abs <= 2e-2 and mean-abs "
-                         "<= 2e-3 against the oracle's float32 list-driven math on the same tiles"}
+            "ok": bool(mismatched == in_band and mx <= 2e-2 and mean <= 2e-3),
+            "criterion": "full-width lists bit-exact per tile except in-band threshold flips "
+                         "(float64 energy within 1e-5 relative of alpha * max); output max-abs "
+                         "<= 2e-2 and mean-abs <= 2e-3 against the oracle's float32 "
+                         "list-driven math on the same tiles"}
 
 
 # ---------------------------------------------------------------------------
@@ -669,7 +705,7 @@ def main(argv=None) -> int:
                 samples.append(smp)
         cpu = {"value": round(fl / dt / 1e12, 6), "unit": "TFLOP/s", "cores": os.cpu_count(),
                "kind": "port", "sample": "; ".join(descs), "seconds": round(dt, 2)}
-        parity = sample_parity(samples, lists_p, out_p, G, cfg.tile_q)
+        parity = sample_parity(samples, lists_p, out_p, G, q, cfg)
         del pk_p, pv_p, lists_p, out_p
 
     if rank == 0:
