@@ -602,6 +602,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float emax = (Mx == -INFINITY || Kx == -INFINITY) ? 0.f : ex2(Kx - Mx);
       const float thr = g.alpha * emax;
       const bool dense_tail = it.t >= max(g.Nt - g.last_n, 0);
+      // (unrolled: the statistics loads and exponentials of four word groups
+      // are independent, so their latencies overlap)
+#pragma unroll 4
       for (int base_b = ew * 32; base_b < Nb; base_b += 128) {
         const int b = base_b + lane;
         const long long bs = (long long)b * g.block_k, be = bs + g.block_k;
@@ -654,6 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar_sync(bar_id, 128);                 // prefixes complete
       if (p.sel_ids != nullptr) {
         const int nsel = totals[0], npr = totals[1];
+#pragma unroll 4
         for (int base_b = ew * 32; base_b < Nb; base_b += 128) {
           const int b = base_b + lane;
           if (b < Nb) {
