@@ -315,10 +315,6 @@ def parse_args(argv=None):
     ap.add_argument("--tile-q", type=int, default=None,
                     help="query positions per selection tile (default: 128 packed rows = 128/G positions)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--reassembly", choices=("auto", "multicast", "peers", "nccl"), default="auto",
-                    help="multi-GPU output reassembly: NVLink multicast stores or per-rank stores "
-                         "from the attention kernel, or an NCCL all-gather after it (auto: multicast "
-                         "where available; FPV2_NO_MULTICAST=1 selects NCCL)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tiles", type=int, default=2048,
                     help="latest tiles of a KV head per CPU sample (the reference arm uses 1/8)")
@@ -531,41 +527,32 @@ def main(argv=None) -> int:
     vs = v[rank * hkv_r:(rank + 1) * hkv_r].contiguous()
     qd, kd, vd = qs.to(dev)[None], ks.to(dev)[None], vs.to(dev)[None]
     out_full = torch.empty((world, hkv_r * G, length, D), dtype=dtype, device=dev) if world > 1 else None
-    # Multi-GPU reassembly: fused into the attention kernel (stores into every
-    # rank's copy of a symmetric-memory buffer: NVLink multicast, or one store per
-    # rank's mapping) where the GPUs can map each other's memory, else NCCL.
+    # Multi-GPU reassembly: fused into the attention kernel (multicast stores into a
+    # symmetric-memory buffer) where the GPUs support NVLink multicast, else NCCL.
     mc = None
-    mode = args.reassembly
-    if mode == "auto":
-        mode = "nccl" if os.environ.get("FPV2_NO_MULTICAST", "0") == "1" else "multicast"
-    if world > 1 and mode != "nccl":
+    if world > 1 and os.environ.get("FPV2_NO_MULTICAST", "0") != "1":
         import torch.distributed as dist
-        from fpv2.shard import _symmetric_buffer
+        from fpv2.shard import _multicast_buffer
 
         good = 1
         try:
-            mc = _symmetric_buffer((world * hkv_r * G, length, D), dtype, dev, None)
-        except Exception as exc:  # no symmetric memory on this node
-            print(f"fused reassembly unavailable ({exc}); using NCCL all-gather", file=sys.stderr)
+            mc = _multicast_buffer((world * hkv_r * G, length, D), dtype, dev, None)
+        except Exception as exc:  # no symmetric memory / multicast on this node
+            print(f"multicast reassembly unavailable ({exc}); using NCCL all-gather",
+                  file=sys.stderr)
             mc, good = None, 0
-        if mc is not None and mode == "multicast" and not mc[2]:
-            mode = "peers"   # no NVLink multicast on these GPUs
         agree = torch.tensor([good], dtype=torch.int32, device=dev)
         dist.all_reduce(agree, op=dist.ReduceOp.MIN)   # every rank takes the same path
         if int(agree.item()) == 0:
             mc = None
-    if mc is None:
-        mode = "nccl" if world > 1 else "none"
-    from fpv2.shard import reassembly_args
-
-    ra_args = reassembly_args(mc, mode, rank * hkv_r * G, world * hkv_r * G) if mc else {}
+    mc_args = (mc[2], rank * hkv_r * G, world * hkv_r * G) if mc else None
 
     def step():
         if mc is not None:
             from fpv2.shard import head_parallel_sdpa
 
             return head_parallel_sdpa(qd, kd, vd, scale=scale, config=base_cfg, fused=True,
-                                      copy=False, reassembly=mode)
+                                      copy=False)
         out = fpv2.fpv2_sdpa(qd, kd, vd, scale=scale, config=base_cfg)
         if world > 1:
             import torch.distributed as dist
@@ -611,7 +598,7 @@ def main(argv=None) -> int:
                                           query_length=length, key_length=length)
         e[1].record(stream)
         out = sparse_attention(qd[0], kd[0], vd[0], pk_, pv_, *lists_, scale=scale, config=cfg,
-                               offset=0, query_length=length, key_length=length, **ra_args)
+                               offset=0, query_length=length, key_length=length, multicast=mc_args)
         e[2].record(stream)
         if mc is not None:
             mc[1].barrier(channel=0)   # every rank's output tiles have landed everywhere
@@ -749,8 +736,8 @@ def main(argv=None) -> int:
             "data": "synthetic topic-block generator (seed 0), inputs resident in HBM",
             "config": {
                 "workload": layer_workload(args, length, Hq, Hkv, D, cfg),
-                "parallelism": (f"head-parallel x{world}, output reassembled by the attention "
-                                f"kernel's stores into every rank's copy ({mode})" if mc is not None else
+                "parallelism": (f"head-parallel x{world}, output reassembled by NVLink multicast "
+                                "stores from the attention kernel" if mc is not None else
                                 f"head-parallel x{world} (+NCCL all-gather of the output)") if world > 1
                                else "single GPU",
                 "l2": "inputs (Q+K+V) larger than the 126 MB L2 at every step",
@@ -758,9 +745,8 @@ def main(argv=None) -> int:
                 "index_stage_ms": round(idx_ms, 4),
                 "attention_ms": round(attn_ms, 4),
                 "allgather_ms": round(gather_ms, 4) if world > 1 else 0.0,
-                "reassembly": ({"multicast": "multicast stores in the attention kernel",
-                                "peers": "per-rank stores in the attention kernel"}[mode]
-                               if mc is not None else "NCCL all-gather") if world > 1 else "none",
+                "reassembly": ("multicast stores in the attention kernel" if mc is not None
+                               else "NCCL all-gather") if world > 1 else "none",
                 "retained_tflop_per_layer": round(flops_layer / 1e12, 4),
                 "dense_causal_tflop_per_layer": round(dense_flops / 1e12, 3),
                 "block_sparsity": round(sparsity, 4),

@@ -23,25 +23,6 @@ constexpr int kMaskWordsMax = 64;           // pooled-entry mask of one work ite
 
 enum : int { KIND_SEL = 0, KIND_POOL = 1, KIND_CORR = 2, KIND_EMPTY = 3, KIND_DONE = 4 };
 
-// The output leaves through every rank's copy of the full output (head-parallel
-// layer) instead of this call's `out`.
-__host__ __device__ __forceinline__ bool remote_out(const AttnArgs& a) {
-  return a.out_mc != nullptr || a.n_peers > 0;
-}
-
-// One finished 16-byte output chunk at byte offset `off` of the full output, to
-// every rank: a single NVLink multicast store (the switch writes every rank's
-// copy, this rank's own included), or one plain store per rank's mapping.
-__device__ __forceinline__ void remote_out_st16(const AttnArgs& a, long long off, uint4 v) {
-  if (a.n_peers > 0) {
-#pragma unroll
-    for (int r = 0; r < AttnArgs::kMaxPeers; ++r)
-      if (r < a.n_peers) *reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.out_peer[r]) + off) = v;
-  } else {
-    multimem_st16(reinterpret_cast<char*>(a.out_mc) + off, v);
-  }
-}
-
 struct Rec {
   int kind;
   int kstart;     // SEL: first key; POOL: first pooled row; CORR: first list entry

@@ -770,7 +770,7 @@ size_t pair_smem_bytes() {
 
 bool attn_pair_supported(const AttnArgs& a) {
   if (!attn_tc_supported(a)) return false;
-  if (remote_out(a)) return false;   // output to every rank stays on attn_tc_kernel
+  if (a.out_mc != nullptr) return false;   // multicast output stays on attn_tc_kernel
   const int nch = (a.G * a.tile_q) / 128;
   const int cpg = a.tile_q >= 128 ? a.tile_q / 128 : 1;
   return nch >= 2 && (nch / cpg) % 2 == 0;

@@ -119,8 +119,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&q_full[i]), 1);
-      // last QK + the output stores (two tensor stores, or eight warps' stores to every rank)
-      mbar_init(smem_u32(&q_empty[i]), 1 + (remote_out(a) ? 8 : 2));
+      // last QK + the output stores (two tensor stores, or eight warps' multicast stores)
+      mbar_init(smem_u32(&q_empty[i]), 1 + (a.out_mc != nullptr ? 8 : 2));
     }
     for (int i = 0; i < kRecs; ++i) {
       mbar_init(smem_u32(&rec_full[i]), 1);
@@ -869,16 +869,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool good = true;
         if (part != nullptr) {
           // nothing staged: release the Q buffer with the store path's arrivals
-          if (remote_out(a)) {
+          if (a.out_mc != nullptr) {
             if (lane == 0) mbar_arrive(smem_u32(&q_empty[qs]));
           } else if (quarter == 0 && lane == 0) {
             mbar_arrive(smem_u32(&q_empty[qs]));
           }
-        } else if (remote_out(a)) {
-          // Output to every rank: every thread of the box's warps copies 16-byte
+        } else if (a.out_mc != nullptr) {
+          // Multicast output: every thread of the box's warps copies 16-byte
           // chunks of the staged box (consecutive threads along a row) to the
-          // same place of every rank's full output (one NVLink multicast store,
-          // or one store per rank).
+          // same place of every rank's full output through the NVLink switch.
           good = mbar_wait(smem_u32(&obar[ob]), wi & 1, wc);
           good = __all_sync(0xffffffffu, good);
           if (good) {
@@ -894,8 +893,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int P = P0 + rr;
               const long long head = a.mc_head_offset + ck.h * a.G + P / a.tile_q;
               const long long pos = (long long)ck.t * a.tile_q + P % a.tile_q;
-              if (ob * 64 + cc * 8 < a.D)   // head_dim 96 runs on the 128-wide tiles
-                remote_out_st16(a, ((head * a.Lq_pad + pos) * a.D + ob * 64 + cc * 8) * 2, v);
+              if (ob * 64 + cc * 8 < a.D) {   // head_dim 96 runs on the 128-wide tiles
+                char* dst = reinterpret_cast<char*>(a.out_mc) +
+                            ((head * a.Lq_pad + pos) * a.D + ob * 64 + cc * 8) * 2;
+                multimem_st16(dst, v);
+              }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&q_empty[qs]));
@@ -927,7 +929,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (stored) {   // output stores complete (and visible to the other GPUs) before the CTA retires
-      if (remote_out(a)) asm volatile("fence.acq_rel.sys;" ::: "memory");
+      if (a.out_mc != nullptr) asm volatile("fence.acq_rel.sys;" ::: "memory");
       else bulk_wait_all();
     }
   }
@@ -996,8 +998,9 @@ __global__ void __launch_bounds__(8 * (D / 8)) attn_combine_kernel(Params p) {
   const long long head = (long long)ck.h * a.G + P / a.tile_q;
   const long long pos = (long long)ck.t * a.tile_q + P % a.tile_q;
   if (c0 < a.D) {   // head_dim 96 runs on the 128-wide tiles
-    if (remote_out(a)) {
-      remote_out_st16(a, (((head + a.mc_head_offset) * a.Lq_pad + pos) * a.D + c0) * 2, v);
+    if (a.out_mc != nullptr) {
+      multimem_st16(reinterpret_cast<char*>(a.out_mc) +
+                        (((head + a.mc_head_offset) * a.Lq_pad + pos) * a.D + c0) * 2, v);
       asm volatile("fence.acq_rel.sys;" ::: "memory");
     } else {
       *reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.out) + ((head * a.Lq_pad + pos) * a.D + c0) * 2) = v;
@@ -1039,7 +1042,7 @@ bool encode_attn_maps(const AttnArgs& a, CUtensorMap (&m)[6]) {
   if (!encode_tmap_3d(&m[0], a.q, a.dt, a.D, a.Lq_pad, a.Hq, 64, box_rows, box_heads))
     return false;
   // (with a multicast output the local tensor map is unused; q stands in for it)
-  if (!encode_tmap_3d(&m[5], remote_out(a) ? a.q : a.out, a.dt, a.D, a.Lq_pad, a.Hq, 64,
+  if (!encode_tmap_3d(&m[5], a.out_mc != nullptr ? a.q : a.out, a.dt, a.D, a.Lq_pad, a.Hq, 64,
                       box_rows, box_heads))
     return false;
   if (a.block_table != nullptr) {   // page pools [pages, page_size, Hkv, D]

@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const bool mc = remote_out(a);   // output to every rank's copy
+  const bool mc = a.out_mc != nullptr;
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(q_full), 1);
@@ -674,8 +674,8 @@ __global__ void __launch_bounds__(kWThreads, 1)
         const long long pos = (long long)ck.t * a.tile_q + P % a.tile_q;
         const uint4 z = make_uint4(0u, 0u, 0u, 0u);
         if (mc) {
-          const long long off = ((head + a.mc_head_offset) * a.Lq_pad + pos) * kD * 2;
-          for (int cc = 0; cc < kD / 8; ++cc) remote_out_st16(a, off + cc * 16, z);
+          char* dst = reinterpret_cast<char*>(a.out_mc) + ((head + a.mc_head_offset) * a.Lq_pad + pos) * kD * 2;
+          for (int cc = 0; cc < kD / 8; ++cc) multimem_st16(dst + cc * 16, z);
           stored = true;
         } else {
           uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.out) + (head * a.Lq_pad + pos) * kD * 2);
@@ -738,7 +738,9 @@ __global__ void __launch_bounds__(kWThreads, 1)
               const int P = P0 + rr;
               const long long head = a.mc_head_offset + ck.h * a.G + P / a.tile_q;
               const long long pos = (long long)ck.t * a.tile_q + P % a.tile_q;
-              remote_out_st16(a, ((head * a.Lq_pad + pos) * kD + ob * 64 + cc * 8) * 2, v);
+              char* dst = reinterpret_cast<char*>(a.out_mc) +
+                          ((head * a.Lq_pad + pos) * kD + ob * 64 + cc * 8) * 2;
+              multimem_st16(dst, v);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(stage_free));
@@ -817,7 +819,7 @@ cudaError_t launch_attn_wide(const AttnArgs& a, const TcLaunch& L, int* sched, c
   CUtensorMap tq, tk, tv, tpk, tpv, to;
   if (!encode_tmap_3d(&tq, a.q, a.dt, a.D, a.Lq_pad, a.Hq, 64, box_rows, box_heads))
     return cudaErrorInvalidValue;
-  if (!encode_tmap_3d(&to, remote_out(a) ? a.q : a.out, a.dt, a.D, a.Lq_pad, a.Hq, 64,
+  if (!encode_tmap_3d(&to, a.out_mc != nullptr ? a.q : a.out, a.dt, a.D, a.Lq_pad, a.Hq, 64,
                       box_rows, box_heads))
     return cudaErrorInvalidValue;
   if (!encode_tmap_3d(&tk, a.k, a.dt, a.D, a.Lk_pad, a.Hkv, 64, 128, 1)) return cudaErrorInvalidValue;

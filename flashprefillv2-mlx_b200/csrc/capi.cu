@@ -442,7 +442,7 @@ int64_t fpv2_select_workspace_bytes(int q_dtype, int k_dtype, int32_t kv_heads,
 namespace fpv2 {
 namespace {
 
-// Shared body of fpv2_sparse_attention, _multicast, _peers and _paged.
+// Shared body of fpv2_sparse_attention and fpv2_sparse_attention_multicast.
 // K/V in page pools (fpv2_sparse_attention_paged); null for contiguous K/V.
 struct PagedKV {
   const int32_t* table;
@@ -458,8 +458,7 @@ int run_sparse_attention(const void* q, const void* k, const void* v, const void
                          int32_t key_length, float scale, int32_t block_k, int32_t tile_q,
                          int32_t mean_correction, void* out, void* out_mc, int32_t head_offset,
                          int32_t heads_total, void* workspace, int64_t workspace_bytes,
-                         void* stream, const PagedKV* paged = nullptr,
-                         void* const* out_peers = nullptr, int32_t n_peers = 0) {
+                         void* stream, const PagedKV* paged = nullptr) {
   if (dtype != DT_F16 && dtype != DT_BF16)
     return fail(FPV2_ERR_INVALID_ARGUMENT, "q, k, and v must share float16 or bfloat16 dtype");
   if (pooled_dtype != dtype && pooled_dtype != DT_F32)
@@ -477,16 +476,11 @@ int run_sparse_attention(const void* q, const void* k, const void* v, const void
     return fail(FPV2_ERR_INVALID_ARGUMENT, "key_length must fit within padded k/v");
   if (offset < 0 || (long long)offset + query_length > key_length)
     return fail(FPV2_ERR_INVALID_ARGUMENT, "offset does not align queries within the key sequence");
-  if (n_peers < 0 || n_peers > AttnArgs::kMaxPeers || (n_peers > 0 && out_peers == nullptr))
-    return fail(FPV2_ERR_INVALID_ARGUMENT, "peer outputs: 1 to 8 rank addresses");
-  for (int r = 0; r < n_peers; ++r)
-    if (out_peers[r] == nullptr || reinterpret_cast<uintptr_t>(out_peers[r]) % 16 != 0)
-      return fail(FPV2_ERR_INVALID_ARGUMENT, "peer output addresses must be non-null and 16-byte aligned");
-  const bool remote = out_mc != nullptr || n_peers > 0;
-  if (!q || !k || !v || (!out && !remote) || !selected_ids || !selected_counts ||
+  if (!q || !k || !v || (!out && !out_mc) || !selected_ids || !selected_counts ||
       (mean_correction && (!pooled_k || !pooled_v || !pruned_ids || !pruned_counts)))
     return fail(FPV2_ERR_INVALID_ARGUMENT, "null tensor pointer");
-  if (remote && (head_offset < 0 || heads_total < q_heads || head_offset > heads_total - q_heads))
+  if (out_mc != nullptr &&
+      (head_offset < 0 || heads_total < q_heads || head_offset > heads_total - q_heads))
     return fail(FPV2_ERR_INVALID_ARGUMENT, "multicast output heads out of range");
   if (paged != nullptr) {
     if (paged->table == nullptr || paged->page_size <= 0 || paged->num_pages <= 0 ||
@@ -527,9 +521,7 @@ int run_sparse_attention(const void* q, const void* k, const void* v, const void
   a.corr = mean_correction ? 1 : 0;
   a.scale_log2 = scale * kLog2e;
   a.corr_shift = (float)log2((double)block_k);
-  a.out_mc = n_peers > 0 ? nullptr : out_mc;
-  a.n_peers = n_peers;
-  for (int r = 0; r < n_peers; ++r) a.out_peer[r] = out_peers[r];
+  a.out_mc = out_mc;
   a.status = d->status;
   a.mc_head_offset = head_offset;
   a.mc_heads = heads_total;
@@ -598,10 +590,9 @@ int run_sparse_attention(const void* q, const void* k, const void* v, const void
     return fail(FPV2_ERR_UNSUPPORTED,
                 "paged K/V needs the tcgen05 path (bf16/fp16, head_dim 64/96/128, aligned, block_k a "
                 "multiple of 128, page_size a multiple of 8 that divides 128 or is a multiple of 128)");
-  } else if (remote) {
+  } else if (out_mc != nullptr) {
     return fail(FPV2_ERR_UNSUPPORTED,
-                "multicast or peer output needs the tcgen05 path (bf16/fp16, head_dim 64/96/128/256, "
-                "aligned)");
+                "multicast output needs the tcgen05 path (bf16/fp16, head_dim 64/96/128/256, aligned)");
   } else {
     e = launch_attn_generic(a, s);
     if (e != cudaSuccess) return cuda_fail(e, "attn_generic launch");
@@ -673,26 +664,6 @@ int fpv2_sparse_attention_multicast(
                                     query_length, key_length, scale, block_k, tile_q,
                                     mean_correction, nullptr, out_multicast, head_offset,
                                     heads_total, workspace, workspace_bytes, stream);
-}
-
-int fpv2_sparse_attention_peers(
-    const void* q, const void* k, const void* v, const void* pooled_k, const void* pooled_v,
-    int pooled_dtype, const int32_t* selected_ids, const int32_t* selected_counts,
-    const int32_t* pruned_ids, const int32_t* pruned_counts, int dtype, int32_t q_heads,
-    int32_t kv_heads, int32_t padded_q_len, int32_t padded_k_len, int32_t head_dim,
-    int32_t offset, int32_t query_length, int32_t key_length, float scale, int32_t block_k,
-    int32_t tile_q, int32_t mean_correction, void* const* out_peers, int32_t n_peers,
-    int32_t head_offset, int32_t heads_total, void* workspace, int64_t workspace_bytes,
-    void* stream) {
-  if (out_peers == nullptr || n_peers <= 0)
-    return fail(FPV2_ERR_INVALID_ARGUMENT, "peer outputs: 1 to 8 rank addresses");
-  return fpv2::run_sparse_attention(q, k, v, pooled_k, pooled_v, pooled_dtype, selected_ids,
-                                    selected_counts, pruned_ids, pruned_counts, dtype, q_heads,
-                                    kv_heads, padded_q_len, padded_k_len, head_dim, offset,
-                                    query_length, key_length, scale, block_k, tile_q,
-                                    mean_correction, nullptr, nullptr, head_offset, heads_total,
-                                    workspace, workspace_bytes, stream, nullptr, out_peers,
-                                    n_peers);
 }
 
 int fpv2_sparse_attention_paged(

@@ -80,13 +80,6 @@ struct AttnArgs {
   void* out_mc = nullptr;
   int mc_head_offset = 0;
   int mc_heads = 0;
-  // Optional peer output (the same reassembly with unicast stores): the base
-  // address of that full output in every rank's memory, this rank's own
-  // included (peer mappings over NVLink); each finished 16-byte chunk is
-  // stored once per rank. Used instead of out_mc when n_peers > 0.
-  static constexpr int kMaxPeers = 8;
-  void* out_peer[kMaxPeers] = {};
-  int n_peers = 0;
   // Optional paged K/V: k and v point at page pools [num_pages, page_size, Hkv,
   // D]; key position p is row p % page_size of page block_table[p / page_size].
   // Null: k and v are [Hkv, Lk_pad, D].

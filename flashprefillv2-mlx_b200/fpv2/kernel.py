@@ -14,8 +14,6 @@ reference's Metal tiling options; the CUDA kernels choose their own tiles.
 
 from __future__ import annotations
 
-import ctypes
-
 import math
 from dataclasses import dataclass
 
@@ -156,7 +154,6 @@ def sparse_attention(
     tile: TileConfig | None = None,
     pack_gqa: bool = False,
     multicast: tuple[int, int, int] | None = None,
-    peers: tuple[tuple[int, ...], int, int] | None = None,
 ) -> torch.Tensor | None:
     """Tiled block-sparse attention with the pooled mean correction.
 
@@ -170,12 +167,7 @@ def sparse_attention(
     head-parallel multi-GPU layer) writes the output into every rank's full
     ``[heads_total, padded_q_len, dim]`` buffer behind an NVLink multicast
     address instead of a new tensor, at head ``head_offset + h``, and returns None.
-    ``peers=(addresses, head_offset, heads_total)`` does the same with one
-    plain store per rank: ``addresses`` holds that buffer's address in every
-    rank's memory as this GPU maps it (its own and its peers', up to 8).
     """
-    if multicast is not None and peers is not None:
-        raise ValueError("pass multicast or peers, not both")
     if q.ndim != 3 or k.ndim != 3 or v.ndim != 3:
         raise ValueError("q, k, and v must have shape [heads, sequence, dim]")
     if k.shape != v.shape:
@@ -242,13 +234,6 @@ def sparse_attention(
         _lib.check(_lib.lib().fpv2_sparse_attention_multicast(
             *args, mc_ptr, head_offset, heads_total, _lib.ptr(workspace), workspace.numel() * 4,
             _lib.stream_of(q)))
-        return None
-    if peers is not None:
-        addrs, head_offset, heads_total = peers
-        arr = (ctypes.c_void_p * len(addrs))(*[int(a) for a in addrs])
-        _lib.check(_lib.lib().fpv2_sparse_attention_peers(
-            *args, arr, len(addrs), head_offset, heads_total, _lib.ptr(workspace),
-            workspace.numel() * 4, _lib.stream_of(q)))
         return None
     out = torch.empty_like(qc)
     _lib.check(_lib.lib().fpv2_sparse_attention(

@@ -113,14 +113,12 @@ def fpv2_sdpa(
     scale: float,
     config: FPV2Config = FPV2Config(),
     multicast: tuple[int, int, int] | None = None,
-    peers: tuple[tuple[int, ...], int, int] | None = None,
 ) -> torch.Tensor | None:
     """Apply FPV2 to an eligible batch-one, bottom-right causal attention (fpv2/patch.py:102-174).
 
-    ``multicast`` or ``peers`` (not in the reference) is forwarded to
-    ``sparse_attention``: the output goes to every rank's buffer (through an
-    NVLink multicast address, or one store per rank's mapping) and the call
-    returns None.
+    ``multicast`` (not in the reference) is forwarded to ``sparse_attention``: the
+    output goes to every rank's buffer behind an NVLink multicast address and
+    the call returns None.
     """
     if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
         raise ValueError("q, k, and v must have shape [batch, heads, sequence, dim]")
@@ -155,7 +153,7 @@ def fpv2_sdpa(
     output = sparse_attention(
         padded_q, padded_k, padded_v, pooled_k, pooled_v, *indices, scale=scale,
         config=config, offset=offset, query_length=query_length, key_length=key_length,
-        pack_gqa=config.pack_gqa, multicast=multicast, peers=peers,
+        pack_gqa=config.pack_gqa, multicast=multicast,
     )
     if output is None:
         return None

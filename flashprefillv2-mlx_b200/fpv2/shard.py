@@ -5,11 +5,9 @@ attention belongs to one KV head (fpv2/selection.py:178-185,
 fpv2/kernel.py:212-256 of the reference), so the layer splits over KV heads with
 no collective inside the hot path: rank r owns KV heads
 ``[r*Hkv/P, (r+1)*Hkv/P)`` and their query heads, runs the fused index stage and
-the sparse attention on them, and the output ``[Hq, L, D]`` is reassembled on
-every rank: by the attention kernel itself, which stores each finished tile
-into every rank's copy over NVLink (multicast or per-rank stores), or by one
-NCCL all-gather after it (any torch.distributed backend works for the host
-logic).
+the sparse attention on them, and a single all-gather reassembles the output
+``[Hq, L, D]`` (NCCL over NVLink/NVSwitch on GPUs; any torch.distributed backend
+works for the host logic).
 """
 
 from __future__ import annotations
@@ -76,13 +74,11 @@ def gather_heads(local: torch.Tensor, group=None, out: torch.Tensor | None = Non
 
 _SYMM_BUFFERS: dict = {}
 
-REASSEMBLY_MODES = ("multicast", "peers", "nccl")
 
-
-def _symmetric_buffer(shape, dtype, device, group):
-    """Full-output buffer in torch symmetric memory, cached per shape. Returns
-    (tensor, handle, the tensor's NVLink multicast address or 0 where the GPUs
-    offer no multicast, the tensor's address in every rank's mapping)."""
+def _multicast_buffer(shape, dtype, device, group):
+    """Full-output buffer in torch symmetric memory, bound to an NVLink multicast
+    object across the group (cached per shape). Returns (tensor, handle,
+    multicast address of the tensor) or None when the GPUs offer no multicast."""
     key = (tuple(shape), dtype, device, id(group))
     if key in _SYMM_BUFFERS:
         return _SYMM_BUFFERS[key]
@@ -91,26 +87,16 @@ def _symmetric_buffer(shape, dtype, device, group):
     grp = group if group is not None else dist.group.WORLD
     buf = symm_mem.empty(*shape, dtype=dtype, device=device)
     handle = symm_mem.rendezvous(buf, grp)
-    # the tensor's offset inside the symmetric allocation is the same in every
-    # rank's mapping and in the multicast mapping
-    off = buf.data_ptr() - int(handle.buffer_ptrs[handle.rank])
-    peers = tuple(int(p) + off for p in handle.buffer_ptrs)
-    mc = 0
+    entry = None
     mc_base = int(getattr(handle, "multicast_ptr", 0) or 0)
-    if mc_base and 0 <= off and off + buf.numel() * buf.element_size() <= int(handle.buffer_size):
-        mc = mc_base + off
-    entry = (buf, handle, mc, peers)
+    if mc_base:
+        # the tensor's offset inside the symmetric allocation is the same in the
+        # local mapping and in the multicast mapping
+        off = buf.data_ptr() - int(handle.buffer_ptrs[handle.rank])
+        if 0 <= off and off + buf.numel() * buf.element_size() <= int(handle.buffer_size):
+            entry = (buf, handle, mc_base + off)
     _SYMM_BUFFERS[key] = entry
     return entry
-
-
-def reassembly_args(entry, mode: str, head_offset: int, heads_total: int) -> dict:
-    """Keyword arguments of ``sparse_attention`` / ``fpv2_sdpa`` that send the
-    output to every rank's copy of ``entry``'s buffer."""
-    _, _, mc, peers = entry
-    if mode == "multicast":
-        return {"multicast": (mc, head_offset, heads_total)}
-    return {"peers": (peers, head_offset, heads_total)}
 
 
 def head_parallel_sdpa(
@@ -123,56 +109,40 @@ def head_parallel_sdpa(
     group=None,
     fused: bool | None = None,
     copy: bool = True,
-    reassembly: str | None = None,
 ) -> torch.Tensor:
     """FPV2 on this rank's head shard (``[1, Hq/P, L, D]``, ``[1, Hkv/P, L, D]``);
     every rank returns the full ``[1, Hq, L, D]`` output.
 
-    Fused (the default on GPUs that can map each other's memory): the attention
+    Fused (the default where the GPUs support NVLink multicast): the attention
     kernel writes each finished output tile straight into every rank's copy of
-    the full output (torch symmetric memory), so the reassembly overlaps the
-    computation -- ``reassembly="multicast"`` through the NVLink multicast
-    address (one store per chunk; the switch writes every copy, this rank's own
-    included), ``"peers"`` with one store per rank's mapping (each GPU's links
-    carry (P-1)/P of the output in each direction, and nothing comes back to
-    its sender). The default is ``FPV2_REASSEMBLY`` if set, else multicast where
-    the GPUs offer it, else peers. That buffer is cached per shape and reused by
-    the next call of the same shape (every layer of a model), so by default the
-    result is copied out of it; ``copy=False`` returns the buffer itself, valid
-    only until the next call with the same shape (for callers that consume the
-    output before the next layer). ``reassembly="nccl"`` (or ``fused=False``):
-    one NCCL all-gather follows the kernel and the result is a fresh tensor."""
-    import os
-
+    the full output through the multicast address (torch symmetric memory), so
+    the reassembly overlaps the computation. That buffer is cached per shape and
+    reused by the next call of the same shape (every layer of a model), so by
+    default the result is copied out of it; ``copy=False`` returns the buffer
+    itself, valid only until the next call with the same shape (for callers that
+    consume the output before the next layer). Otherwise one NCCL all-gather
+    follows the kernel and the result is a fresh tensor either way."""
     from fpv2 import _lib
     from fpv2.patch import _effective_config
 
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     hq, lq, d = q.shape[1], q.shape[2], q.shape[3]
     eff = _effective_config(config, hq, k.shape[1])
-    mode = reassembly or os.environ.get("FPV2_REASSEMBLY") or "multicast"
-    if mode not in REASSEMBLY_MODES:
-        raise ValueError(f"reassembly must be one of {REASSEMBLY_MODES}")
-    capable = (world > 1 and eff is not None and q.is_cuda
-               and dist.get_backend(group) == "nccl"
-               and bool(_lib.fast_path_mask(q.dtype, hq, k.shape[1], d, eff.block_k, eff.tile_q,
-                                            1) & 2))
-    if fused is False or not capable:
-        mode = "nccl"
+    if fused is None:
+        fused = (world > 1 and eff is not None and q.is_cuda
+                 and dist.get_backend(group) == "nccl"
+                 and _lib.fast_path_mask(q.dtype, hq, k.shape[1], d, eff.block_k, eff.tile_q, 1) & 2)
     entry = None
-    if mode != "nccl":
+    if fused:
         lq_pad = (lq + eff.tile_q - 1) // eff.tile_q * eff.tile_q
-        entry = _symmetric_buffer((world * hq, lq_pad, d), q.dtype, q.device, group)
-        if mode == "multicast" and not entry[2]:
-            mode = "peers"   # no NVLink multicast on these GPUs
+        entry = _multicast_buffer((world * hq, lq_pad, d), q.dtype, q.device, group)
     if entry is None:
         local = fpv2_sdpa(q, k, v, scale=scale, config=config)
         return gather_heads(local, group)
-    buf, handle = entry[0], entry[1]
+    buf, handle, mc_addr = entry
     rank = dist.get_rank(group)
     handle.barrier(channel=0)   # no rank still reads the previous contents
-    fpv2_sdpa(q, k, v, scale=scale, config=config,
-              **reassembly_args(entry, mode, rank * hq, world * hq))
+    fpv2_sdpa(q, k, v, scale=scale, config=config, multicast=(mc_addr, rank * hq, world * hq))
     handle.barrier(channel=0)   # every rank's tiles have landed in every buffer
     out = buf[None, :, :lq, :]
     return out.clone() if copy else out

@@ -223,27 +223,6 @@ FPV2_API int fpv2_sparse_attention_multicast(
     int32_t heads_total, void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
- * fpv2_sparse_attention_multicast with unicast stores (no counterpart in the
- * reference): `out_peers` is a host array of `n_peers` (1 to 8) device
- * addresses, the same full output [heads_total, padded_q_len, head_dim] in
- * every rank's memory as this GPU maps it (this rank's own buffer and peer
- * mappings over NVLink, e.g. the buffer pointers of a torch symmetric-memory
- * handle). Each finished 16-byte output chunk is stored once per rank, so each
- * GPU's NVLink carries (n_peers - 1) / n_peers of the output out and in,
- * where a multicast store also brings the rank's own share back in through
- * the switch. Same requirements and cross-rank ordering as the multicast call.
- */
-FPV2_API int fpv2_sparse_attention_peers(
-    const void* q, const void* k, const void* v, const void* pooled_k, const void* pooled_v,
-    int pooled_dtype, const int32_t* selected_ids, const int32_t* selected_counts,
-    const int32_t* pruned_ids, const int32_t* pruned_counts, int dtype, int32_t q_heads,
-    int32_t kv_heads, int32_t padded_q_len, int32_t padded_k_len, int32_t head_dim,
-    int32_t offset, int32_t query_length, int32_t key_length, float scale, int32_t block_k,
-    int32_t tile_q, int32_t mean_correction, void* const* out_peers, int32_t n_peers,
-    int32_t head_offset, int32_t heads_total, void* workspace, int64_t workspace_bytes,
-    void* stream);
-
-/*
  * fpv2_sparse_attention for callers that cannot allocate device memory (no
  * counterpart in the reference). Same arguments as fpv2_sparse_attention
  * without the workspace, and the results that call gives with a workspace of

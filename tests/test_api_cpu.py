@@ -56,23 +56,6 @@ def test_invalid_arguments_return_status_without_gpu():
     assert "divisible" in _lib.lib().fpv2_last_error().decode()
 
 
-def test_peer_output_arguments_are_checked_without_gpu():
-    f = _lib.lib().fpv2_sparse_attention_peers
-    bf16 = _lib.dtype_code(torch.bfloat16)
-
-    def call(addrs):
-        arr = (ctypes.c_void_p * max(1, len(addrs)))(*addrs) if addrs else None
-        return f(None, None, None, None, None, bf16, None, None, None, None, bf16, 8, 2, 256, 256,
-                 128, 0, 256, 256, 0.1, 128, 32, 1, arr, len(addrs), 0, 8, None, 0, None)
-
-    assert call([]) == _lib.ERR_INVALID_ARGUMENT
-    assert "1 to 8" in _lib.lib().fpv2_last_error().decode()
-    assert call([4096] * 9) == _lib.ERR_INVALID_ARGUMENT
-    assert "1 to 8" in _lib.lib().fpv2_last_error().decode()
-    assert call([4096, 4096 + 8]) == _lib.ERR_INVALID_ARGUMENT
-    assert "16-byte aligned" in _lib.lib().fpv2_last_error().decode()
-
-
 def test_cpu_tensors_are_rejected():
     with pytest.raises(ValueError, match="CUDA"):
         fpv2.pool_blocks(torch.zeros(2, 8, 4), 4)
