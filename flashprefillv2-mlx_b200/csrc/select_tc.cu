@@ -79,13 +79,16 @@ struct Item {
 __device__ __forceinline__ Item make_item(const Params& p, int w) {
   const SelectGeom& g = p.g;
   Item it;
-  it.h = w % g.Hkv;
-  it.t = g.Nt - 1 - w / g.Hkv;
+  // (unsigned 32-bit divisions: every role derives each item's geometry on its
+  // own critical path, and end <= offset + valid_lq < 2^32 always fits)
+  it.h = (int)((unsigned)w % (unsigned)g.Hkv);
+  it.t = g.Nt - 1 - (int)((unsigned)w / (unsigned)g.Hkv);
   it.tile_first = (long long)g.offset + (long long)it.t * g.tile_q;
   it.tile_last = min(it.tile_first + g.tile_q, (long long)g.offset + g.valid_lq) - 1;
   it.n_full = 0;
-  if (it.tile_last + 1 >= g.block_k)
-    it.n_full = (int)min((long long)g.Nb, (it.tile_last + 1) / g.block_k);
+  const long long end = it.tile_last + 1;
+  if (end >= g.block_k)
+    it.n_full = (int)min((unsigned)g.Nb, (unsigned)end / (unsigned)g.block_k);
   it.n_mt = (it.n_full + 127) / 128;
   const bool all_rows_valid = (long long)(it.t + 1) * g.tile_q <= g.valid_lq;
   const bool all_see_all =
