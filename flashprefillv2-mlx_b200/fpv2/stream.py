@@ -13,6 +13,13 @@ The copies in set the pace, so the last chunk is cut again into query slices
 slice keeps the dense tail), which leaves only the last slice's kernels and
 copy out after the last byte has come in.
 
+The device staging buffers (two sets of one chunk's q, k and v) are kept per
+device for the next call of the same shapes, so a call's first copies in only
+wait for the previous call's kernels that read the same set, not for its last
+kernels and copies out: back-to-back calls (consecutive layers or requests)
+overlap one call's tail with the next call's copies in. ``release_staging``
+frees them.
+
 The result equals ``fpv2_sdpa`` on the whole tensors bit for bit whenever the
 attention kernel splits the same long work items over KV segments in both (a
 choice made per launch from the number of work items; where it differs the
@@ -27,6 +34,29 @@ from dataclasses import replace
 
 from fpv2.patch import _effective_config, fpv2_sdpa
 from fpv2.selection import FPV2Config
+
+
+# device -> [key, buffer sets, events after which each set is free]
+_STAGING: dict = {}
+
+
+def release_staging(device: torch.device | None = None) -> None:
+    """Drop the staging buffers kept by ``sdpa_from_host`` (all devices by
+    default); the caching allocator takes them back once their queued copies
+    and kernels are done."""
+    if device is None:
+        _STAGING.clear()
+    else:
+        _STAGING.pop(torch.device(device), None)
+
+
+def _staging(device, key, make):
+    entry = _STAGING.get(device)
+    if entry is not None and entry[0] == key:
+        return entry, False
+    entry = [key, make(), [None, None]]
+    _STAGING[device] = entry
+    return entry, True
 
 
 def sdpa_from_host(
@@ -90,23 +120,28 @@ def sdpa_from_host(
     h2d = torch.cuda.Stream(device)
     d2h = torch.cuda.Stream(device)
     # two buffer sets: chunk c uses set c % 2
-    bufs = []
-    with torch.cuda.device(device):
-        for _ in range(min(2, nchunks)):
-            qb = torch.empty((1, cs * g) + tuple(q.shape[2:]), dtype=q.dtype, device=device)
-            kb = torch.empty((1, cs) + tuple(k.shape[2:]), dtype=k.dtype, device=device)
-            vb = torch.empty((1, cs) + tuple(v.shape[2:]), dtype=v.dtype, device=device)
-            for t in (qb, kb, vb):
-                t.record_stream(h2d)
-            bufs.append((qb, kb, vb))
-    # The buffers come from the compute stream's pool, which only orders their
-    # reuse with the compute stream: blocks still read by kernels queued there
-    # (the previous call's lists, scratch, inputs) may be handed out again. The
-    # copy stream starts after the compute stream's queued work for that reason.
-    ready = torch.cuda.Event()
-    ready.record(compute)
-    h2d.wait_event(ready)
-    inputs_free: list[torch.cuda.Event | None] = [None, None]
+    def make():
+        sets = []
+        with torch.cuda.device(device):
+            for _ in range(min(2, nchunks)):
+                sets.append((torch.empty((1, cs * g) + tuple(q.shape[2:]), dtype=q.dtype, device=device),
+                             torch.empty((1, cs) + tuple(k.shape[2:]), dtype=k.dtype, device=device),
+                             torch.empty((1, cs) + tuple(v.shape[2:]), dtype=v.dtype, device=device)))
+        return sets
+
+    key = (cs, g, tuple(q.shape[2:]), tuple(k.shape[2:]), q.dtype, k.dtype, nchunks > 1)
+    entry, fresh = _staging(device, key, make)
+    bufs, inputs_free = entry[1], entry[2]
+    for t in (x for st in bufs for x in st):
+        t.record_stream(h2d)   # this call's copy stream writes them
+    if fresh:
+        # New buffers come from the compute stream's pool, which only orders their
+        # reuse with the compute stream: blocks still read by kernels queued there
+        # may be handed out again, so the copy stream starts after that queued work.
+        # Kept buffers only wait for the previous call's kernels that read them.
+        ready = torch.cuda.Event()
+        ready.record(compute)
+        h2d.wait_event(ready)
     last = None
     for c in range(nchunks):
         b = c % 2
@@ -114,8 +149,8 @@ def sdpa_from_host(
         hs = slice(c * cs * g, (c + 1) * cs * g)
         ks = slice(c * cs, (c + 1) * cs)
         if c == nchunks - 1 and len(bounds) > 1:
-            last = _stream_sliced(q, k, v, out, qb, kb, vb, hs, ks, bounds, offset, scale, config,
-                                  compute, h2d, d2h, inputs_free[b])
+            last, inputs_free[b] = _stream_sliced(q, k, v, out, qb, kb, vb, hs, ks, bounds, offset,
+                                                  scale, config, compute, h2d, d2h, inputs_free[b])
             break
         with torch.cuda.stream(h2d):
             if inputs_free[b] is not None:
@@ -146,7 +181,9 @@ def _stream_sliced(q, k, v, out, qb, kb, vb, hs, ks, bounds, offset, scale, conf
                    compute, h2d, d2h, inputs_free):
     """The last chunk in query slices: its K and V come in first, then the query
     rows slice by slice (one copy per head: a slice is strided across heads);
-    slice i runs as soon as its rows have arrived and goes out right after."""
+    slice i runs as soon as its rows have arrived and goes out right after.
+    Returns the event of the last copy out and that of the last kernels that
+    read the buffer set."""
     heads = range(hs.start, hs.stop)
     loaded = []
     with torch.cuda.stream(h2d):
@@ -179,4 +216,4 @@ def _stream_sliced(q, k, v, out, qb, kb, vb, hs, ks, bounds, offset, scale, conf
             last = torch.cuda.Event()
             last.record(d2h)
         o.record_stream(d2h)
-    return last
+    return last, done
