@@ -265,3 +265,30 @@ def test_workspace_size_queries_without_gpu():
     assert bf16 - f16 == conv
     assert f16 >= _lib.ATTN_WORKSPACE_BYTES
     assert L.fpv2_attention_workspace_bytes(_lib.F32, *args, _lib.F32, 1) >= _lib.ATTN_WORKSPACE_BYTES
+
+
+def test_streaming_staging_buffers_are_kept_per_device_and_shape():
+    """sdpa_from_host keeps one entry of staging buffers per device: the same
+    key reuses it, another key replaces it, release_staging drops it."""
+    from fpv2 import stream
+
+    stream.release_staging()
+    made = []
+
+    def make():
+        made.append(1)
+        return [("q", "k", "v")]
+
+    dev = torch.device("cuda", 0)
+    e1, fresh1 = stream._staging(dev, ("a",), make)
+    e2, fresh2 = stream._staging(dev, ("a",), make)
+    assert fresh1 and not fresh2 and e1 is e2 and len(made) == 1
+    assert e1[2] == [None, None]
+    e3, fresh3 = stream._staging(dev, ("b",), make)
+    assert fresh3 and e3 is not e1 and len(stream._STAGING) == 1
+    stream._staging(torch.device("cuda", 1), ("a",), make)
+    assert len(stream._STAGING) == 2
+    stream.release_staging(dev)
+    assert list(stream._STAGING) == [torch.device("cuda", 1)]
+    stream.release_staging()
+    assert not stream._STAGING
