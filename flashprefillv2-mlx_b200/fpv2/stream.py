@@ -106,15 +106,9 @@ def sdpa_from_host(
     nchunks = hkv // cs
     lq, lk = q.shape[2], k.shape[2]
     offset = lk - lq
-    # Query slices of the last chunk: cut points on multiples of 128 rows and of
-    # the selection tile, and the final slice holds at least the dense-tail tiles.
     eff = _effective_config(config, hq, hkv)
     unit = max(128, eff.tile_q * max(1, eff.last_n_blocks)) if eff is not None else lq
-    unit = (unit + 127) // 128 * 128
-    cuts = sorted({(i * lq // tail_slices) // unit * unit for i in range(1, tail_slices)} - {0})
-    while cuts and lq - cuts[-1] < unit:
-        cuts.pop()
-    bounds = list(zip([0] + cuts, cuts + [lq])) if offset >= 0 else [(0, lq)]
+    bounds = _slice_bounds(lq, tail_slices, unit) if offset >= 0 else [(0, lq)]
 
     compute = torch.cuda.current_stream(device)
     h2d = torch.cuda.Stream(device)
@@ -175,6 +169,17 @@ def sdpa_from_host(
     if last is not None:
         compute.wait_event(last)
     return out
+
+
+def _slice_bounds(lq: int, tail_slices: int, unit: int) -> list[tuple[int, int]]:
+    """Query slices [s0, s1) of the last chunk: about ``tail_slices`` equal
+    parts, cut on multiples of ``unit`` rounded up to 128 rows (the selection
+    tile and the dense tail), the final slice at least one unit long."""
+    unit = (unit + 127) // 128 * 128
+    cuts = sorted({(i * lq // tail_slices) // unit * unit for i in range(1, tail_slices)} - {0})
+    while cuts and lq - cuts[-1] < unit:
+        cuts.pop()
+    return list(zip([0] + cuts, cuts + [lq]))
 
 
 def _stream_sliced(q, k, v, out, qb, kb, vb, hs, ks, bounds, offset, scale, config,

@@ -292,3 +292,18 @@ def test_streaming_staging_buffers_are_kept_per_device_and_shape():
     assert list(stream._STAGING) == [torch.device("cuda", 1)]
     stream.release_staging()
     assert not stream._STAGING
+
+
+@pytest.mark.parametrize("lq,slices,unit", [(65536, 4, 64), (2048, 4, 64), (1920, 4, 64),
+                                            (2048, 3, 300), (200, 4, 64), (65536, 1, 64),
+                                            (4096, 16, 256)])
+def test_streaming_query_slices_cover_the_rows_on_unit_boundaries(lq, slices, unit):
+    from fpv2.stream import _slice_bounds
+
+    b = _slice_bounds(lq, slices, unit)
+    u = (unit + 127) // 128 * 128
+    assert b[0][0] == 0 and b[-1][1] == lq
+    assert all(s1 == t0 for (_, s1), (t0, _) in zip(b, b[1:]))   # contiguous, no overlap
+    assert all(s0 % u == 0 and s1 > s0 for s0, s1 in b)
+    assert b[-1][1] - b[-1][0] >= min(u, lq)                      # the dense tail stays whole
+    assert len(b) <= slices
