@@ -613,6 +613,9 @@ def main(argv=None) -> int:
 
         dist.barrier()
     torch.cuda.synchronize()
+    from fpv2 import _lib as fpv2_lib
+
+    launches0 = fpv2_lib.launch_count()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         start.record(stream)
@@ -620,11 +623,14 @@ def main(argv=None) -> int:
             step_timed(ev[i])
         end.record(stream)
         torch.cuda.synchronize()
+    launches = fpv2_lib.launch_count() - launches0   # this rank's kernels in the timed region
     if world > 1:
         import torch.distributed as dist
 
         dist.barrier()
-    from fpv2 import _lib as fpv2_lib
+        lt = torch.tensor([launches], dtype=torch.int64, device=dev)
+        dist.all_reduce(lt)   # every rank's launches: the whole job's
+        launches = int(lt.item())
 
     status = fpv2_lib.device_status(dev)
     if status:
@@ -778,7 +784,7 @@ def main(argv=None) -> int:
             "cpu_baseline": cpu,
             "parity": parity,
             "e2e": e2e,
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": launches,
             "clocks": clocks.summary(),
         }
         emit_json(line)

@@ -805,6 +805,7 @@ cudaError_t launch_attn_pair(const AttnArgs& a, const TcLaunch& L, int* sched, c
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
     if (e != cudaSuccess) return e;                                                         \
     attn_pair_kernel<DD, TT, VV><<<grid, kThreads, smem, stream>>>(m[0], m[1], m[2], m[3], m[4], p); \
+    count_launch();                                                                         \
   }
   if (a.D == 64 && a.dt == DT_BF16 && vdt == DT_F16) FPV2_PAIR_LAUNCH(64, DT_BF16, DT_F16)
   else if (a.D == 64 && a.dt == DT_BF16) FPV2_PAIR_LAUNCH(64, DT_BF16, DT_BF16)

@@ -1162,7 +1162,11 @@ cudaError_t launch_attn_tc_impl(const AttnArgs& a, const TcLaunch& L, void* work
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
     if (e != cudaSuccess) return e;                                                         \
     attn_tc_kernel<DD, TT, VV, GG><<<grid, kThreads, smem, stream>>>(m[0], m[1], m[2], m[3], m[4], m[5], p); \
-    if (p.split.max_slots > 0) attn_combine_kernel<DD, TT><<<cgrid, DD, 0, stream>>>(p);     \
+    count_launch();                                                                         \
+    if (p.split.max_slots > 0) {                                                            \
+      attn_combine_kernel<DD, TT><<<cgrid, DD, 0, stream>>>(p);                             \
+      count_launch();                                                                       \
+    }                                                                                       \
   }
 #define FPV2_ATTN_TYPES(DD)                                                                 \
   {                                                                                         \

@@ -846,6 +846,7 @@ cudaError_t launch_attn_wide(const AttnArgs& a, const TcLaunch& L, int* sched, c
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
     if (e != cudaSuccess) return e;                                                         \
     attn_wide_kernel<TT, VV><<<grid, kWThreads, smem, stream>>>(tq, tk, tv, tpk, tpv, to, p); \
+    count_launch();                                                                         \
   }
   if (a.dt == DT_BF16 && vdt == DT_F16) FPV2_WIDE_LAUNCH(DT_BF16, DT_F16)
   else if (a.dt == DT_BF16) FPV2_WIDE_LAUNCH(DT_BF16, DT_BF16)

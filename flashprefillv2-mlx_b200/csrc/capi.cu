@@ -8,6 +8,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -221,6 +222,10 @@ static int run_select(const SelectGeom& g, const void* q, int q_dt, const void* 
   return FPV2_OK;
 }
 
+std::atomic<long long> g_launch_count{0};
+
+void count_launch() { g_launch_count.fetch_add(1, std::memory_order_relaxed); }
+
 }  // namespace fpv2
 
 using namespace fpv2;
@@ -228,6 +233,8 @@ using namespace fpv2;
 extern "C" {
 
 int fpv2_version(void) { return 100; }
+
+int64_t fpv2_launch_count(void) { return g_launch_count.load(std::memory_order_relaxed); }
 
 const char* fpv2_last_error(void) { return t_last_error.c_str(); }
 

@@ -113,6 +113,8 @@ cudaError_t launch_v_to_f16(const VConvArgs& a, cudaStream_t stream) {
   const dim3 grid(std::max(bx, 1), a.Hkv);
   v_to_f16_kernel<<<grid, kConvThreads, 0, stream>>>(a);
   v_rescale_kernel<<<grid, kConvThreads, 0, stream>>>(a);
+  count_launch();
+  count_launch();
   return cudaGetLastError();
 }
 

@@ -355,6 +355,7 @@ cudaError_t launch_select_generic(const SelectGeom& g, const void* q, int q_dt, 
   if (nblk == 0) return cudaSuccess;
   select_generic_kernel<<<(unsigned)nblk, kSelThreads, smem, stream>>>(g, q, q_dt, pk, pk_dt,
                                                                        mask, lists);
+  count_launch();
   return cudaGetLastError();
 }
 
@@ -364,6 +365,7 @@ cudaError_t launch_raw_scores(const SelectGeom& g, const void* q, int q_dt, cons
   if (rows == 0) return cudaSuccess;
   raw_scores_kernel<<<(unsigned)rows, 128, sizeof(float) * g.D, stream>>>(g, q, q_dt, pk, pk_dt,
                                                                           out);
+  count_launch();
   return cudaGetLastError();
 }
 
@@ -376,6 +378,7 @@ cudaError_t launch_compact(const uint8_t* mask, int Hkv, int Nt, int Nb, int blo
   const int blocks = (rows * 32 + threads - 1) / threads;
   compact_kernel<<<blocks, threads, 0, stream>>>(mask, rows, Nt, Nb, block_k, tile_q, offset,
                                                  valid_lk, sel_ids, sel_counts, pr_ids, pr_counts);
+  count_launch();
   return cudaGetLastError();
 }
 
@@ -390,6 +393,7 @@ cudaError_t launch_attn_generic(const AttnArgs& a, cudaStream_t stream) {
     attn_generic_kernel<DT_F16><<<blocks, kAttnWarps * 32, smem, stream>>>(a);
   else
     return cudaErrorInvalidValue;
+  count_launch();
   return cudaGetLastError();
 }
 

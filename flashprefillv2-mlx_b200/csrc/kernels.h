@@ -28,6 +28,10 @@ struct PagedPoolArgs {
 cudaError_t launch_pool_pages(const PagedPoolArgs& a, int dt_in, int dt_out, cudaStream_t stream);
 
 // ---- selection geometry shared by all selection kernels -----------------
+// Host-side count of the kernels this library has launched (every launch
+// site calls it once per launch; read with fpv2_launch_count).
+void count_launch();
+
 struct SelectGeom {
   int Hq, Hkv, G, Lq_pad, Nb, D, Nt;
   int offset, valid_lq, valid_lk;

@@ -209,6 +209,7 @@ cudaError_t launch_pool_t(const PoolArgs& a, int ntensors, cudaStream_t stream) 
       const int64_t units = nblocks * ntensors;
       const int g = (int)std::min<int64_t>(units, 2 * (int64_t)sms);   // two CTAs per SM
       pool_pipe_kernel<DT_IN, DT_OUT><<<g, kPipeThreads, smem, stream>>>(a, ntensors);
+      count_launch();
       return cudaGetLastError();
     }
    }
@@ -222,10 +223,12 @@ cudaError_t launch_pool_t(const PoolArgs& a, int ntensors, cudaStream_t stream) 
     if (smem > 48 * 1024) vec = false;
     else {
       pool_vec_kernel<DT_IN, DT_OUT><<<grid, kPoolThreads, smem, stream>>>(a);
+      count_launch();
       return cudaGetLastError();
     }
   }
   pool_scalar_kernel<DT_IN, DT_OUT><<<grid, kPoolThreads, 0, stream>>>(a);
+  count_launch();
   return cudaGetLastError();
 }
 
@@ -284,6 +287,7 @@ cudaError_t launch_pool_pages_t(const PagedPoolArgs& a, cudaStream_t stream) {
   const int nblocks = a.heads * (a.length / a.bs);
   const size_t smem = sizeof(double) * (size_t)(kPoolThreads / cpr) * a.D;
   pool_pages_kernel<DT_IN, DT_OUT><<<nblocks, kPoolThreads, smem, stream>>>(a);
+  count_launch();
   return cudaGetLastError();
 }
 

@@ -773,6 +773,7 @@ cudaError_t launch_select_tc(const SelectTcArgs& a, const void* q, const void* p
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
     if (e != cudaSuccess) return e;                                                            \
     kern<<<grid, kThreads, smem, stream>>>(tq, tk, p);                                         \
+    count_launch();                                                                            \
   }
   if (g.D == 64) FPV2_SELECT_LAUNCH(64)
   else if (g.D == 256) FPV2_SELECT_LAUNCH(256)
@@ -859,6 +860,7 @@ cudaError_t launch_pk_split3(const float* pk, void* out, int dt, int Hkv, int Nb
   if (e != cudaSuccess) return e;
   const int gx = (int)std::max<long long>(1, std::min<long long>((per_head + 255) / 256, 64));
   pk_absmax_kernel<<<dim3(gx, Hkv), 256, 0, stream>>>(pk, amax, per_head);
+  count_launch();
   const int grid = (int)std::max<long long>(1, std::min<long long>((n + 255) / 256, 4096));
   if (dt == DT_BF16)
     pk_split3_kernel<DT_BF16><<<grid, 256, 0, stream>>>(pk, out, amax, ex, Hkv, per_head);
@@ -866,6 +868,7 @@ cudaError_t launch_pk_split3(const float* pk, void* out, int dt, int Hkv, int Nb
     pk_split3_kernel<DT_F16><<<grid, 256, 0, stream>>>(pk, out, amax, ex, Hkv, per_head);
   else
     return cudaErrorInvalidValue;
+  count_launch();
   return cudaGetLastError();
 }
 

@@ -28,6 +28,7 @@ __global__ void wait_selftest_kernel(int* status, long long budget) {
 
 cudaError_t launch_wait_selftest(const TcLaunch& L, cudaStream_t stream) {
   wait_selftest_kernel<<<1, 32, 0, stream>>>(L.status, L.budget);
+  count_launch();
   return cudaGetLastError();
 }
 

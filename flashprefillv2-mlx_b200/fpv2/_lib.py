@@ -32,6 +32,7 @@ _DTYPE_CODES = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32}
 # Every exported entry point with its ctypes signature.
 _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "fpv2_version": (ctypes.c_int, []),
+    "fpv2_launch_count": (ctypes.c_int64, []),
     "fpv2_last_error": (ctypes.c_char_p, []),
     "fpv2_device_supported": (ctypes.c_int, [ctypes.c_int]),
     "fpv2_device_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int32)]),
@@ -193,6 +194,11 @@ def require_cuda(*tensors: torch.Tensor) -> None:
             dev = t.device
         elif t.device != dev:
             raise ValueError("all tensors must be on the same CUDA device")
+
+
+def launch_count() -> int:
+    """Kernels the library has launched in this process so far (``fpv2_launch_count``)."""
+    return int(lib().fpv2_launch_count())
 
 
 def device_status(device: torch.device | int | None = None, clear: bool = True) -> int:

@@ -53,6 +53,13 @@ FPV2_API int fpv2_version(void);
 /* Message of the calling thread's most recent failed call ("" if none). */
 FPV2_API const char* fpv2_last_error(void);
 
+/*
+ * Kernels this library has launched in this process, all devices and threads
+ * (no counterpart in the reference): the difference across a region of calls
+ * is how many of the library's kernels ran there.
+ */
+FPV2_API int64_t fpv2_launch_count(void);
+
 /* FPV2_OK when `device` is an sm_100 GPU this build can run on. */
 FPV2_API int fpv2_device_supported(int device);
 

@@ -569,3 +569,24 @@ def test_v_beyond_fp16_range_is_rescaled():
     assert torch.isfinite(outb).all()
     mx, mean = P.kernel_errors(outb / (2.0 ** 17), P.np32(out))
     assert mx <= 2 ** -7 and mean <= 1e-6, (mx, mean)
+
+
+def test_launch_count_counts_the_library_kernels():
+    """fpv2_launch_count rises by the kernels each call launches: the index stage
+    is one pooling launch (K and V) and one selection launch; the attention is the
+    fp16 copy of V and its range check, the attention kernel and, when long work
+    items split over segments, the combine kernel."""
+    q, k, v = topic_qkv(length=4096, query_heads=8, kv_heads=2, seed=63, dtype=torch.bfloat16)
+    cfg = _effective_config(fpv2.FPV2Config(alpha=0.1), 8, 2)
+    scale = 128 ** -0.5
+    qg, kg, vg = cuda(q, k, v)
+    c0 = _lib.launch_count()
+    pk, pv, lists, _ = fpv2.index_stage(qg, kg, vg, scale=scale, config=cfg, offset=0,
+                                        query_length=4096, key_length=4096)
+    c1 = _lib.launch_count()
+    fpv2.sparse_attention(qg, kg, vg, pk, pv, *lists, scale=scale, config=cfg)
+    c2 = _lib.launch_count()
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    assert c1 - c0 == 2
+    assert c2 - c1 in (4, 5)
