@@ -28,9 +28,10 @@ outputs differ by rounding only, well inside the output tolerance).
 
 from __future__ import annotations
 
-import torch
-
+import threading
 from dataclasses import replace
+
+import torch
 
 from fpv2.patch import _effective_config, fpv2_sdpa
 from fpv2.selection import FPV2Config
@@ -38,16 +39,20 @@ from fpv2.selection import FPV2Config
 
 # device -> [key, buffer sets, events after which each set is free]
 _STAGING: dict = {}
+# Calls from several host threads queue their work one at a time, so each call
+# sees the events of the call before it on the same kept buffers.
+_STAGING_LOCK = threading.RLock()
 
 
 def release_staging(device: torch.device | None = None) -> None:
     """Drop the staging buffers kept by ``sdpa_from_host`` (all devices by
     default); the caching allocator takes them back once their queued copies
     and kernels are done."""
-    if device is None:
-        _STAGING.clear()
-    else:
-        _STAGING.pop(torch.device(device), None)
+    with _STAGING_LOCK:
+        if device is None:
+            _STAGING.clear()
+        else:
+            _STAGING.pop(torch.device(device), None)
 
 
 def _staging(device, key, make):
@@ -79,8 +84,15 @@ def sdpa_from_host(
     makes ``out`` readable. Copies from or to pageable host memory still work but
     do not overlap. ``tail_slices`` (1 = off) cuts the last chunk into that many
     query slices, on boundaries that are multiples of the selection tile and of
-    128 rows.
+    128 rows. Calls from several host threads queue their work one at a time.
     """
+    with _STAGING_LOCK:
+        return _sdpa_from_host(q, k, v, scale=scale, config=config, out=out,
+                               kv_heads_per_chunk=kv_heads_per_chunk, device=device,
+                               tail_slices=tail_slices)
+
+
+def _sdpa_from_host(q, k, v, *, scale, config, out, kv_heads_per_chunk, device, tail_slices):
     for name, t in (("q", q), ("k", k), ("v", v)):
         if t.device.type != "cpu":
             raise ValueError(f"{name} must be a host tensor; use fpv2_sdpa for device tensors")
