@@ -111,7 +111,9 @@ def _sdpa_from_host(q, k, v, *, scale, config, out, kv_heads_per_chunk, device, 
         out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
     elif out.device.type != "cpu" or out.shape != q.shape or out.dtype != q.dtype or not out.is_contiguous():
         raise ValueError("out must be a contiguous host tensor shaped and typed like q")
-    if device is None:
+    # one key per GPU for the kept buffers, whichever form the caller names it in
+    device = torch.device("cuda") if device is None else torch.device(device)
+    if device.index is None:
         device = torch.device("cuda", torch.cuda.current_device())
     g = hq // hkv
     cs = kv_heads_per_chunk
