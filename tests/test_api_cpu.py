@@ -51,9 +51,11 @@ def test_fast_path_selection_rules_without_gpu():
 
 
 def test_invalid_arguments_return_status_without_gpu():
+    before = _lib.launch_count()
     rc = _lib.lib().fpv2_pool_blocks(None, 1, 2, 7, 4, 4, None, 1, None)
     assert rc == _lib.ERR_INVALID_ARGUMENT
     assert "divisible" in _lib.lib().fpv2_last_error().decode()
+    assert _lib.launch_count() == before   # a rejected call launches nothing
 
 
 def test_cpu_tensors_are_rejected():
